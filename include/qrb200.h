@@ -1,0 +1,92 @@
+/*
+ * qrb200 -- batched Householder QR for NVIDIA B200 (sm_100a), C ABI.
+ *
+ * Drop-in boundary for the reference operator ``custom_kernel(data) -> (H, tau)``
+ * (Raymondlol/qr-v2-b200-kernel ``submission.py:560-596``; contract of the harness that
+ * calls it: ``harness/eval.py:189-211``, output checks ``harness/reference.py:175-204``).
+ *
+ * Layout (identical to torch.geqrf / LAPACK sgeqrf, row-major storage):
+ *   A    : batch matrices, each n x n float32 row-major (row stride n), matrix b at
+ *          A + b * a_batch_stride (a_batch_stride >= n*n elements). Read only.
+ *   H    : batch x n x n float32 row-major, contiguous. R = triu(H); reflector j is
+ *          v_j = (0,..,0, 1, H[j+1:, j]) with the unit diagonal implicit.
+ *   tau  : batch x n float32, contiguous. Q = H_0 H_1 ... H_{n-1}, H_j = I - tau_j v_j v_j^T.
+ * Sign convention: beta = -sign(alpha) * ||(alpha, x)||, tau = (beta - alpha)/beta,
+ * tau = 0 when x == 0 (submission.py:91-107, LAPACK slarfg without rescaling).
+ *
+ * Execution: every call is asynchronous on ``stream`` (a cudaStream_t; NULL = legacy
+ * default stream), makes no host synchronisation and allocates no memory: scratch comes
+ * from the caller's ``workspace`` (size from qrb200_workspace_bytes, 256-byte aligned).
+ * Two calls that share a workspace must be ordered on the same stream.
+ *
+ * Every entry point returns a status (QRB200_OK = 0). Device-side failures found by a
+ * bounded wait are reported by qrb200_device_status() after the stream has completed.
+ */
+#ifndef QRB200_H_
+#define QRB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  QRB200_OK = 0,
+  QRB200_ERR_ARG = 1,        /* bad shape, stride or null pointer                    */
+  QRB200_ERR_WORKSPACE = 2,  /* workspace too small or not 256-byte aligned          */
+  QRB200_ERR_CUDA = 3,       /* a CUDA runtime call or kernel launch failed          */
+  QRB200_ERR_DEVICE = 4,     /* current device is not an sm_100 (B200-class) GPU     */
+  QRB200_ERR_TIMEOUT = 5     /* a device-side bounded wait expired (see device_status) */
+};
+
+/* Bytes of scratch that qrb200_geqrf_f32 needs for (batch, n).
+ * Replaces the per-call temporaries the reference allocates through torch
+ * (submission.py:177-185 H clone + tau, :453-480 V/G/M/W/Y). */
+size_t qrb200_workspace_bytes(int64_t batch, int64_t n);
+
+/* Batched QR: H, tau <- geqrf(A). Replaces custom_kernel (submission.py:560-596) and
+ * its back-ends _fused_qr (:177-185), _factor_custom (:520-553) and torch.geqrf (:576, :583).
+ * A is not modified (the reference clones it first, submission.py:179, :522). */
+int qrb200_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                     int64_t a_batch_stride, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Human-readable text for a status code (static storage). */
+const char* qrb200_status_string(int status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int qrb200_version(void);
+
+/* Device-side error word of the current device (0 = none), cleared by the read.
+ * Uses a synchronous symbol copy (it waits for prior work on the legacy default stream);
+ * call it after the stream that ran the QR has completed. */
+int qrb200_device_status(int* status_out);
+
+/* ---- diagnostics (no counterpart in the reference; used by bench.py) ---------------- */
+
+/* Number of kernels this library has launched in the process so far (all threads). */
+long long qrb200_launch_count(void);
+
+/* Per-kernel-kind totals of one profiled call. */
+typedef struct qrb200_kernel_stat {
+  char name[32];        /* kernel kind, e.g. "panel_factor", "wy_upd"                 */
+  int32_t launches;     /* launches of this kind in the call                          */
+  int32_t tensor_bound; /* 1: compute (FLOP) bound contraction, 0: memory/latency     */
+  double ms;            /* summed CUDA-event duration of those launches               */
+  double flops;         /* algorithmic FLOPs of those launches                         */
+  double bytes;         /* algorithmic HBM bytes of those launches                     */
+} qrb200_kernel_stat;
+
+/* Same computation as qrb200_geqrf_f32, with a CUDA event pair around every launch; waits
+ * for the stream, then fills up to max_stats entries (one per kernel kind that ran). */
+int qrb200_profile_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                             int64_t a_batch_stride, void* workspace, size_t workspace_bytes,
+                             void* stream, qrb200_kernel_stat* stats, int max_stats, int* n_stats);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRB200_H_ */

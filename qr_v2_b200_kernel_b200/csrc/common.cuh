@@ -1,0 +1,52 @@
+// Shared device helpers for the qrb200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qrb200 {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// Transposed butterfly reduction of NV per-lane partial sums across a warp.
+// On return d[0 .. NV/32) of lane L hold the warp-wide sums of the original entries
+// L*(NV/32) + q. Each of the five xor steps halves the live array: the lane keeps the
+// half selected by its own bit and adds the partner's copy of that half, so the whole
+// reduction costs NV*31/32 shuffles instead of 5*NV for NV independent reductions.
+template <int NV>
+__device__ __forceinline__ void warp_transpose_reduce(float (&d)[NV], int lane) {
+  static_assert(NV % 32 == 0, "NV must be a multiple of 32");
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int o = 16 >> step;
+    const int half = (NV >> step) >> 1;
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int q = 0; q < half; ++q) {
+      const float send = up ? d[q] : d[q + half];
+      const float keep = up ? d[q + half] : d[q];
+      d[q] = keep + __shfl_xor_sync(kFullMask, send, o);
+    }
+  }
+}
+
+// Householder reflector scalars for pivot alpha and squared tail norm xnorm2
+// (LAPACK sign convention, no rescaling -- the same arithmetic as the reference panel).
+struct Reflector {
+  float diag;   // new diagonal: beta when a reflector is needed, alpha otherwise
+  float tau;    // (beta - alpha) / beta, or 0
+  float scale;  // 1 / (alpha - beta), or 0: v_tail = x * scale
+};
+
+__device__ __forceinline__ Reflector make_reflector(float alpha, float xnorm2) {
+  Reflector r;
+  const float nrm = sqrtf(fmaf(alpha, alpha, xnorm2));
+  const float beta = alpha >= 0.f ? -nrm : nrm;
+  const bool need = xnorm2 > 0.f;
+  r.diag = need ? beta : alpha;
+  r.tau = need ? (beta - alpha) / beta : 0.f;
+  r.scale = need ? 1.f / (alpha - beta) : 0.f;
+  return r;
+}
+
+}  // namespace qrb200

@@ -1,0 +1,312 @@
+// qrb200 C ABI: argument checking, workspace layout and the per-panel launch schedule.
+//
+// Schedule (right-looking blocked Householder, panel width NB = 32), per panel k:
+//   panel_factor_kernel  -- cluster of CP CTAs per matrix, panel + tau + T      (1 launch)
+//   trailing update      -- C <- C - V T^T V^T C on the columns right of the panel
+//                           (wy_vtc / wy_tw / wy_upd, 3 launches)
+// Small matrices (n <= 64) are factored whole by one CTA in a single launch (the panel
+// kernel with the panel width equal to n), which is the fused one-CTA-per-matrix path.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "../../include/qrb200.h"
+#include "panel.cuh"
+#include "wy_simt.cuh"
+
+namespace qrb200 {
+
+constexpr int kNB = 32;              // panel width of the blocked path
+constexpr int kPanelThreads = 256;   // threads per panel CTA
+constexpr int kPanelRPT = 2;         // panel rows per thread
+constexpr int kPanelRows = kPanelThreads * kPanelRPT;  // rows per panel CTA
+constexpr int kMaxCluster = 8;       // portable cluster size
+constexpr int kMaxN = kPanelRows * kMaxCluster;        // 4096
+constexpr int kSmallN = 64;          // whole-matrix single-CTA path up to this order
+
+__device__ int g_device_status = 0;
+
+// ---------------------------------------------------------------------------------------
+// Launch accounting. Every kernel launch goes through LaunchScope, which counts it and,
+// while a profiling call is active on this host thread, brackets it with CUDA events and
+// records its algorithmic flops and bytes.
+enum KernelKind { K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_NUM_KINDS };
+static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc",
+                                                   "wy_tw", "wy_upd"};
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1};
+
+static std::atomic<long long> g_launches{0};
+
+struct ProfRecord {
+  int kind;
+  cudaEvent_t start, stop;
+  double flops, bytes;
+};
+struct ProfSession {
+  cudaStream_t stream;
+  std::vector<ProfRecord> recs;
+};
+static thread_local ProfSession* t_prof = nullptr;
+
+struct LaunchScope {
+  int kind;
+  double flops, bytes;
+  cudaEvent_t a = nullptr, b = nullptr;
+  LaunchScope(int kd, double f, double by) : kind(kd), flops(f), bytes(by) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (t_prof) {
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      cudaEventRecord(a, t_prof->stream);
+    }
+  }
+  ~LaunchScope() {
+    if (t_prof) {
+      cudaEventRecord(b, t_prof->stream);
+      t_prof->recs.push_back({kind, a, b, flops, bytes});
+    }
+  }
+};
+
+// Algorithmic work of one Householder panel (LAPACK xGEQR2 count) per matrix.
+static double panel_flops(double m, double w) { return 2.0 * m * w * w - 2.0 * w * w * w / 3.0; }
+
+static inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
+static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Row splits of the V^T C product for panel k: enough CTAs to cover the GPU twice.
+static int choose_nsplit(long long batch, int n, int k, int w) {
+  const int m = n - k, nc = n - k - w;
+  if (nc <= 0) return 1;
+  const long long tiles = (long long)cdiv(nc, 64) * batch;
+  int ns = (int)std::min<long long>(8, std::max<long long>(1, (296 + tiles - 1) / tiles));
+  ns = std::min(ns, std::max(1, m / 128));
+  return ns;
+}
+
+static int max_nsplit(long long batch, int n) {
+  int mx = 1;
+  for (int k = 0; k < n; k += kNB) mx = std::max(mx, choose_nsplit(batch, n, k, std::min(kNB, n - k)));
+  return mx;
+}
+
+struct Workspace {
+  float* T;
+  float* Wp;
+  float* W2;
+  size_t bytes;
+};
+
+static Workspace layout(long long batch, int n, void* base) {
+  Workspace ws{};
+  const size_t t_bytes = align_up((size_t)batch * kNB * kNB * sizeof(float), 256);
+  const size_t w_elems = (size_t)batch * kNB * (size_t)n;
+  const int ns = max_nsplit(batch, n);
+  const size_t wp_bytes = align_up(w_elems * ns * sizeof(float), 256);
+  const size_t w2_bytes = align_up(w_elems * sizeof(float), 256);
+  char* p = static_cast<char*>(base);
+  ws.T = reinterpret_cast<float*>(p);
+  ws.Wp = reinterpret_cast<float*>(p + t_bytes);
+  ws.W2 = reinterpret_cast<float*>(p + t_bytes + wp_bytes);
+  ws.bytes = (n <= kSmallN) ? 0 : t_bytes + wp_bytes + w2_bytes;
+  return ws;
+}
+
+static int check_device() {
+  static int cached = -1;
+  if (cached >= 0) return cached;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QRB200_ERR_CUDA;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return QRB200_ERR_CUDA;
+  cached = (major == 10) ? QRB200_OK : QRB200_ERR_DEVICE;
+  return cached;
+}
+
+template <int NBT, int NT, int RPT, bool HAS_T>
+static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, panel_factor_kernel<NBT, NT, RPT, HAS_T>, pp);
+}
+
+// Whole-matrix factorisation by one CTA (n <= 64): the panel kernel with width n.
+static cudaError_t run_small(const float* A, float* H, float* tau, long long batch, int n,
+                             long long abs, cudaStream_t s) {
+  PanelParams pp{A, abs, H, tau, nullptr, n, 0, n};
+  LaunchScope ls(K_SMALL, batch * 4.0 * n * (double)n * n / 3.0, batch * 8.0 * n * (double)n);
+  if (n <= 32) return launch_panel<32, 32, 1, false>(pp, 1, batch, s);
+  return launch_panel<64, 64, 1, false>(pp, 1, batch, s);
+}
+
+static cudaError_t run_blocked(const float* A, float* H, float* tau, long long batch, int n,
+                               long long abs, const Workspace& ws, cudaStream_t s) {
+  const int ncmax = n;
+  for (int k = 0; k < n; k += kNB) {
+    const int w = std::min(kNB, n - k);
+    const int m = n - k;
+    const int nc = n - k - w;
+    const float* src = (k == 0) ? A : H;
+    const long long sbs = (k == 0) ? abs : (long long)n * n;
+    const int cluster = cdiv(m, kPanelRows);
+    PanelParams pp{src, sbs, H, tau, nc > 0 ? ws.T : nullptr, n, k, w};
+    cudaError_t e;
+    {
+      LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+      e = launch_panel<kNB, kPanelThreads, kPanelRPT, true>(pp, cluster, batch, s);
+    }
+    if (e != cudaSuccess) return e;
+    if (nc <= 0) continue;
+    WyParams wp{};
+    wp.src = src;
+    wp.src_bstride = sbs;
+    wp.H = H;
+    wp.T = ws.T;
+    wp.Wp = ws.Wp;
+    wp.W2 = ws.W2;
+    wp.n = n;
+    wp.k = k;
+    wp.w = w;
+    wp.nsplit = choose_nsplit(batch, n, k, w);
+    wp.rows_per_split = cdiv(cdiv(m, wp.nsplit), 32) * 32;
+    wp.ncmax = ncmax;
+    const double bm = (double)batch * m;
+    {
+      LaunchScope ls(K_VTC, 2.0 * bm * w * nc, 4.0 * bm * (w + nc) + 4.0 * batch * wp.nsplit * w * (double)nc);
+      wy_vtc_kernel<kNB><<<dim3(cdiv(nc, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
+    }
+    {
+      LaunchScope ls(K_TW, (double)batch * w * w * nc, 4.0 * batch * (wp.nsplit + 1.0) * w * nc);
+      wy_tw_kernel<kNB><<<dim3(cdiv(nc, 128), (unsigned)batch), 128, 0, s>>>(wp);
+    }
+    {
+      LaunchScope ls(K_UPD, 2.0 * bm * w * nc, 8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * w * (double)nc);
+      wy_upd_kernel<kNB><<<dim3(cdiv(nc, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace qrb200
+
+using namespace qrb200;
+
+static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                      int64_t a_batch_stride, void* workspace, size_t workspace_bytes, void* stream);
+
+extern "C" {
+
+size_t qrb200_workspace_bytes(int64_t batch, int64_t n) {
+  if (batch <= 0 || n <= 0 || n > kMaxN) return 0;
+  return layout(batch, (int)n, nullptr).bytes;
+}
+
+int qrb200_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                     int64_t a_batch_stride, void* workspace, size_t workspace_bytes, void* stream) {
+  return geqrf_impl(A, H, tau, batch, n, a_batch_stride, workspace, workspace_bytes, stream);
+}
+
+long long qrb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int qrb200_profile_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                             int64_t a_batch_stride, void* workspace, size_t workspace_bytes,
+                             void* stream, qrb200_kernel_stat* stats, int max_stats, int* n_stats) {
+  if (!stats || !n_stats || max_stats < 0) return QRB200_ERR_ARG;
+  ProfSession sess;
+  sess.stream = static_cast<cudaStream_t>(stream);
+  t_prof = &sess;
+  const int st = geqrf_impl(A, H, tau, batch, n, a_batch_stride, workspace, workspace_bytes, stream);
+  t_prof = nullptr;
+  cudaError_t e = cudaStreamSynchronize(sess.stream);
+  qrb200_kernel_stat acc[K_NUM_KINDS];
+  std::memset(acc, 0, sizeof(acc));
+  for (int k = 0; k < K_NUM_KINDS; ++k) {
+    std::strncpy(acc[k].name, kKindName[k], sizeof(acc[k].name) - 1);
+    acc[k].tensor_bound = kKindTensorBound[k];
+  }
+  for (auto& r : sess.recs) {
+    float ms = 0.f;
+    if (e == cudaSuccess) cudaEventElapsedTime(&ms, r.start, r.stop);
+    acc[r.kind].launches += 1;
+    acc[r.kind].ms += ms;
+    acc[r.kind].flops += r.flops;
+    acc[r.kind].bytes += r.bytes;
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  int cnt = 0;
+  for (int k = 0; k < K_NUM_KINDS && cnt < max_stats; ++k)
+    if (acc[k].launches > 0) stats[cnt++] = acc[k];
+  *n_stats = cnt;
+  if (st != QRB200_OK) return st;
+  return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
+}
+
+}  // extern "C"
+
+static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                      int64_t a_batch_stride, void* workspace, size_t workspace_bytes, void* stream) {
+  if (batch < 0 || n < 0) return QRB200_ERR_ARG;
+  if (batch == 0 || n == 0) return QRB200_OK;
+  if (n > kMaxN || batch > 65535) return QRB200_ERR_ARG;
+  if (!A || !H || !tau) return QRB200_ERR_ARG;
+  if (a_batch_stride < n * n) return QRB200_ERR_ARG;
+  const int dev_ok = check_device();
+  if (dev_ok != QRB200_OK) return dev_ok;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (n <= kSmallN) {
+    e = run_small(A, H, tau, batch, (int)n, a_batch_stride, s);
+  } else {
+    const Workspace ws = layout(batch, (int)n, workspace);
+    if (workspace_bytes < ws.bytes || !workspace) return QRB200_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return QRB200_ERR_WORKSPACE;
+    e = run_blocked(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
+  }
+  if (e != cudaSuccess) return QRB200_ERR_CUDA;
+  return QRB200_OK;
+}
+
+extern "C" {
+
+const char* qrb200_status_string(int status) {
+  switch (status) {
+    case QRB200_OK: return "ok";
+    case QRB200_ERR_ARG: return "invalid argument (shape, stride or null pointer)";
+    case QRB200_ERR_WORKSPACE: return "workspace too small or not 256-byte aligned";
+    case QRB200_ERR_CUDA: return "CUDA runtime error or kernel launch failure";
+    case QRB200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
+    case QRB200_ERR_TIMEOUT: return "device-side bounded wait expired";
+    default: return "unknown status";
+  }
+}
+
+int qrb200_version(void) { return 100; }
+
+int qrb200_device_status(int* status_out) {
+  if (!status_out) return QRB200_ERR_ARG;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return QRB200_ERR_CUDA;
+  const int zero = 0;
+  if (v != 0 && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return QRB200_ERR_CUDA;
+  *status_out = v;
+  return QRB200_OK;
+}
+
+}  // extern "C"

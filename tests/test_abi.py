@@ -1,0 +1,80 @@
+"""C-ABI library: loads, exports every symbol include/qrb200.h declares, host-side checks.
+
+No kernel runs here (CPU-only): only calls that return before touching the device.
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from qr_v2_b200_kernel_b200 import _lib, build
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _header_symbols():
+    text = open(os.path.join(REPO, "include", "qrb200.h")).read()
+    return sorted(set(re.findall(r"\b(qrb200_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_binding_table():
+    assert _header_symbols() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_header_symbol(lib):
+    for name in _header_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_status_strings_and_version(lib):
+    assert lib.qrb200_version() >= 100
+    for st in range(6):
+        assert lib.qrb200_status_string(st)
+    assert lib.qrb200_status_string(0) == b"ok"
+
+
+def test_workspace_query(lib):
+    assert lib.qrb200_workspace_bytes(0, 128) == 0
+    assert lib.qrb200_workspace_bytes(8, 64) == 0  # single-CTA path needs no scratch
+    assert lib.qrb200_workspace_bytes(640, 512) > 0
+    assert lib.qrb200_workspace_bytes(2, 4096) % 256 == 0
+    assert lib.qrb200_workspace_bytes(1, 1 << 20) == 0  # unsupported order
+
+
+def test_argument_errors_before_any_device_work(lib):
+    p = ctypes.c_void_p(16)
+    f = lib.qrb200_geqrf_f32
+    assert f(p, p, p, -1, 8, 64, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert f(p, p, p, 1, -8, 64, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert f(None, p, p, 1, 8, 64, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert f(p, p, p, 2, 8, 63, None, 0, None) == _lib.QRB200_ERR_ARG  # batch stride < n*n
+    assert f(p, p, p, 1, 1 << 20, 1 << 40, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert f(p, p, p, 0, 8, 64, None, 0, None) == _lib.QRB200_OK  # empty batch: no-op
+    assert f(p, p, p, 4, 0, 0, None, 0, None) == _lib.QRB200_OK
+
+
+def test_device_status_null_pointer(lib):
+    assert lib.qrb200_device_status(None) == _lib.QRB200_ERR_ARG
+
+
+def test_operator_rejects_bad_inputs_on_cpu():
+    import torch
+
+    from qr_v2_b200_kernel_b200 import custom_kernel
+
+    with pytest.raises(RuntimeError):
+        custom_kernel(torch.zeros(2, 4, 4))  # CPU tensor: no fallback
+    with pytest.raises(TypeError):
+        custom_kernel(torch.zeros(2, 4, 4, dtype=torch.float64))
+    with pytest.raises(ValueError):
+        custom_kernel(torch.zeros(2, 4, 5))
+    with pytest.raises(TypeError):
+        custom_kernel([[1.0]])

@@ -1,0 +1,149 @@
+"""CUDA path parity: the C-ABI operator against the oracle, the golden fixtures and the
+reference correctness gate (harness/reference.py:189-273), on the B200.
+
+Tolerances (floating point, from the north-star criteria):
+* gate: per matrix ||triu(H) - Q^T A||_1 <= 20 n eps32 ||A||_1 and ||Q^T Q - I||_1 <= 100 n eps32;
+* |diag R| vs torch.geqrf and vs the oracle within the factor bound (scaled <= 20);
+* elementwise H vs the oracle / LAPACK within 20 n eps32 ||A||_1 on well-conditioned inputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qr_v2_b200_kernel_b200 import checker, custom_kernel, gen
+
+pytestmark = pytest.mark.gpu
+
+WELL_CONDITIONED = {"dense", "band", "upper", "diagonal", "rowscale", "clustered"}
+
+
+def _run(A):
+    A_copy = A.clone()
+    H, tau = custom_kernel(A)
+    torch.cuda.synchronize()
+    assert torch.equal(A, A_copy), "input was modified"
+    return H, tau
+
+
+def _assert_gate(A, H, tau, what=""):
+    res = checker.check(A, H, tau)
+    assert res["ok"], (what, res["message"])
+    return res
+
+
+def _assert_diag(A, H, what=""):
+    Hg, _ = torch.geqrf(A)
+    d = checker.compare_diag_r(A, H, Hg)
+    assert d["ok"], (what, d)
+
+
+def test_golden_fixtures(golden):
+    z, meta = golden
+    for c in meta["cases"]:
+        k = c["key"]
+        A = torch.from_numpy(z[k + "_A"]).cuda()
+        H, tau = _run(A)
+        _assert_gate(A, H, tau, c["args"])
+        Hn, taun = H.cpu().numpy(), tau.cpu().numpy()
+        n = A.shape[-1]
+        dl = np.abs(np.abs(np.diagonal(Hn, axis1=1, axis2=2)) - np.abs(np.diagonal(z[k + "_H_lapack"], axis1=1, axis2=2)))
+        sc = np.abs(z[k + "_A"]).sum(axis=-2).max(axis=-1)[:, None] * n * oracle.EPS32
+        assert (dl / np.maximum(sc, 1e-30)).max() <= 20.0, c["args"]
+        if c["args"].get("case", "dense") in WELL_CONDITIONED:
+            tol = 20.0 * n * oracle.EPS32 * sc.max() / (n * oracle.EPS32)
+            assert np.abs(Hn - z[k + "_H_ref"]).max() <= tol, c["args"]
+            assert np.abs(taun - z[k + "_tau_lapack"]).max() <= 1e-4, c["args"]
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 17, 31, 32, 33, 63, 64, 65, 96, 127, 128, 129, 200, 255, 256, 257, 300])
+def test_against_oracle_sizes(n):
+    rng = np.random.default_rng(1000 + n)
+    b = 3
+    A_np = rng.standard_normal((b, n, n)).astype(np.float32)
+    A = torch.from_numpy(A_np).cuda()
+    H, tau = _run(A)
+    Ho, tauo = oracle.geqrf_blocked(A_np)
+    ok, info = oracle.check(A_np, H.cpu().numpy(), tau.cpu().numpy())
+    assert ok, info
+    scale = np.abs(A_np).sum(axis=-2).max(axis=-1)[:, None, None]
+    d = np.abs(H.cpu().numpy() - Ho) / scale
+    assert d.max() <= 20.0 * n * oracle.EPS32, d.max()
+    assert np.abs(tau.cpu().numpy() - tauo).max() <= 1e-4
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C4", "C5"])
+def test_benchmark_configs_full_size(name):
+    A = gen.config_input(name, device="cuda")
+    H, tau = _run(A)
+    _assert_gate(A, H, tau, name)
+    _assert_diag(A, H, name)
+
+
+@pytest.mark.parametrize("idx", range(22))
+def test_reference_test_cases(idx):
+    c = gen.REFERENCE_TEST_CASES[idx]
+    A = gen.generate_input(**c, device="cuda")
+    H, tau = _run(A)
+    _assert_gate(A, H, tau, c)
+
+
+def test_edge_matrices():
+    n = 96
+    cases = {
+        "zero": torch.zeros(2, n, n),
+        "identity": torch.eye(n).expand(2, n, n).clone(),
+        "neg_identity": -torch.eye(n).expand(2, n, n).clone(),
+        "zero_column": torch.randn(2, n, n).index_fill_(2, torch.tensor([5, 40]), 0.0),
+        "rank_one": torch.randn(2, n, 1) @ torch.randn(2, 1, n),
+        "tiny": torch.randn(2, n, n) * 1e-20,
+        "huge": torch.randn(2, n, n) * 1e15,
+    }
+    for name, A in cases.items():
+        A = A.float().cuda().contiguous()
+        H, tau = _run(A)
+        assert torch.isfinite(H).all() and torch.isfinite(tau).all(), name
+        _assert_gate(A, H, tau, name)
+    # the zero matrix: every reflector is the identity
+    H, tau = _run(torch.zeros(1, 40, 40, device="cuda"))
+    assert (tau == 0).all() and (H == 0).all()
+
+
+def test_noncontiguous_and_batch_views():
+    base = torch.randn(6, 160, 160, device="cuda")
+    At = base.transpose(1, 2)  # non-contiguous view
+    H, tau = _run(At)
+    _assert_gate(At.contiguous(), H, tau, "transposed")
+    sub = base[1:4]  # contiguous sub-batch with an offset
+    H2, tau2 = _run(sub)
+    H3, tau3 = _run(sub.clone())
+    assert torch.equal(H2, H3) and torch.equal(tau2, tau3)
+
+
+def test_deterministic_and_batch_independent():
+    A = gen.config_input("C2", device="cuda", batch=12)
+    H1, t1 = _run(A)
+    H2, t2 = _run(A)
+    assert torch.equal(H1, H2) and torch.equal(t1, t2)
+    # a matrix's result does not depend on its batch neighbours
+    H3, t3 = _run(A[5:6].contiguous())
+    assert torch.equal(H3[0], H1[5]) and torch.equal(t3[0], t1[5])
+
+
+def test_runs_on_current_stream():
+    A = gen.config_input("C3", device="cuda", batch=4)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        H, tau = custom_kernel(A)
+    s.synchronize()
+    _assert_gate(A, H, tau, "side stream")
+
+
+def test_error_paths_on_gpu():
+    from qr_v2_b200_kernel_b200._lib import QRB200Error
+
+    with pytest.raises(QRB200Error):
+        custom_kernel(torch.zeros(1, 4097, 4097, device="cuda"))
+    H, tau = custom_kernel(torch.zeros(0, 8, 8, device="cuda"))
+    assert H.shape == (0, 8, 8) and tau.shape == (0, 8)
