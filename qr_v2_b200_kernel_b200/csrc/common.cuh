@@ -38,14 +38,21 @@ struct Reflector {
   float scale;  // 1 / (alpha - beta), or 0: v_tail = x * scale
 };
 
+// With nrm = ||(alpha, x)|| and beta = -sign(alpha) nrm the two quotients simplify to
+//   tau   = (beta - alpha) / beta = 1 + |alpha| / nrm,
+//   scale = 1 / (alpha - beta)    = sign(alpha) / (|alpha| + nrm),
+// so the reflector needs one square root and two independent correctly rounded reciprocals
+// (a ~100-cycle dependent chain instead of a square root and two IEEE divisions in series).
 __device__ __forceinline__ Reflector make_reflector(float alpha, float xnorm2) {
   Reflector r;
   const float nrm = sqrtf(fmaf(alpha, alpha, xnorm2));
-  const float beta = alpha >= 0.f ? -nrm : nrm;
+  const float aa = fabsf(alpha);
   const bool need = xnorm2 > 0.f;
-  r.diag = need ? beta : alpha;
-  r.tau = need ? (beta - alpha) / beta : 0.f;
-  r.scale = need ? 1.f / (alpha - beta) : 0.f;
+  const float inv = __frcp_rn(aa + nrm);
+  const float rn = __frcp_rn(nrm);
+  r.diag = need ? (alpha >= 0.f ? -nrm : nrm) : alpha;
+  r.tau = need ? fmaf(aa, rn, 1.f) : 0.f;
+  r.scale = need ? (alpha >= 0.f ? inv : -inv) : 0.f;
   return r;
 }
 

@@ -1,27 +1,28 @@
 // Householder panel factorisation (larfg + larf over the panel) with the LARFT T factor
 // built in the same pass.
 //
-// One thread-block cluster of CP CTAs factors the m x w panel H[k:n, k:k+w] of one matrix.
-// CTA p of the cluster holds panel rows [p*R, (p+1)*R) in registers (R = NT*RPT rows, one
-// row per thread per RPT slot, all NBT columns of a row in one thread). For every column j:
+// Layout: one warp per panel column. A CTA has 32 warps; warp c owns panel column c, and
+// its lanes hold the CTA's rows of that column, lane l holding local rows l + 32 i
+// (i < RPL). A thread-block cluster of CP CTAs covers a panel taller than 32 * RPL rows,
+// CTA p holding rows [p*R, (p+1)*R), R = 32 * RPL.
 //
-//   1. each thread accumulates d_c = sum_{rows r > j} a[r][j] * a[r][c] for all c < NBT:
-//      c > j are the dot products of the unscaled tail x_j with the trailing panel columns,
-//      c == j is ||x_j||^2 and c < j are x_j . v_c, the LARFT column (V^T v_j);
-//   2. d is reduced over the CTA (warp transposed butterfly + one shared-memory pass) and,
-//      for CP > 1, over the cluster through distributed shared memory (one cluster barrier
-//      per column, partial slots double-buffered by column parity);
-//   3. every thread derives beta, tau and the scale 1/(alpha - beta) from alpha = a[j][j]
-//      and ||x||^2 (reference arithmetic, submission.py:91-107), then applies
-//      a[r][c] -= tau * v_r * (a[j][c] + scale * d_c) to its rows (v_r = scale * a[r][j],
-//      v_j = 1), which is the rank-1 update of submission.py:100-103 with v^T a_c
-//      assembled from the reduced dots;
-//   4. one warp of CTA 0 appends column j of T:
-//      T[:j, j] = -tau_j T[:j, :j] z, z_c = a[j][c] + scale * d_c = v_c . v_j
-//      (the LARFT recurrence of submission.py:129-137 fed by the same reduction).
-//
-// The panel therefore costs one block reduction (plus one cluster barrier when CP > 1) per
-// reflector, reads and writes the panel once, and needs no separate Gram (V^T V) pass.
+// Reflector j (the loop over columns is a runtime loop: the body is a few hundred bytes):
+//   (a) warp j, whose column already carries every earlier reflector, publishes the
+//       unscaled tail x_j (rows below j, zero elsewhere) in shared memory; lane j of every
+//       warp publishes its row-j value a[j][c];
+//   (b) __syncthreads;
+//   (c) every warp c forms d_c = x_j . a_c over its rows and reduces it across the warp:
+//       c > j gives the trailing dots, c == j gives ||x_j||^2 and c < j gives x_j . v_c,
+//       the LARFT column; for CP > 1 the per-CTA sums are added across the cluster through
+//       distributed shared memory after ONE cluster barrier;
+//   (d) every warp derives beta, tau and scale = 1/(alpha - beta) from alpha = a[j][j] and
+//       ||x_j||^2 (the reference arithmetic, submission.py:91-107); warps c > j apply
+//       a_c -= tau * v_j (v_j^T a_c) with v_j^T a_c = a[j][c] + scale * d_c (the rank-1
+//       update of submission.py:100-103); warp j scales its tail into v_j, stores tau and
+//       appends column j of T: T[i][j] = -tau_j sum_{i<=c<j} T[i][c] z_c,
+//       z_c = v_c^T v_j = a[j][c] + scale * d_c (LARFT, submission.py:129-137).
+// Shared slots are double-buffered by the parity of j, so each reflector costs two CTA
+// barriers (one of them the cluster barrier when CP > 1) and no extra Gram pass.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -32,170 +33,313 @@ namespace qrb200 {
 
 namespace cg = cooperative_groups;
 
+constexpr int kPanelW = 32;        // panel width (columns) == warps per panel CTA
+constexpr int kPanelThreads = 1024;
+
 struct PanelParams {
-  const float* src;      // panel source matrix batch (A for the first panel, else H)
-  long long src_bstride; // elements between matrices of src
-  float* H;              // output batch, n x n row-major, contiguous
-  float* tau;            // batch x n
-  float* T;              // batch x NBT x NBT upper-triangular T factors (may be null)
-  int n;                 // matrix order
-  int k;                 // first panel column (== first panel row)
-  int w;                 // panel width, <= NBT
+  const float* src;       // panel source matrix batch (A for the first panel, else H)
+  long long src_bstride;  // elements between matrices of src
+  float* H;               // output batch, n x n row-major, contiguous
+  float* tau;             // batch x n
+  float* T;               // batch x 32 x 32 upper-triangular T factors (may be null)
+  int n;                  // matrix order
+  int k;                  // first panel column (== first panel row)
+  int w;                  // panel width, <= 32
 };
 
-template <int NBT, int NT, int RPT, bool HAS_T>
-__global__ void __launch_bounds__(NT, 1) panel_factor_kernel(PanelParams P) {
-  constexpr int NW = NT / 32;
-  constexpr int Q = NBT / 32;
-  constexpr int R = NT * RPT;
-  static_assert(NBT % 32 == 0 && NT % 32 == 0, "shape");
-  static_assert(NBT <= R, "the diagonal block must sit in the first CTA");
+template <int RPL>
+struct PanelShared {
+  float xs[2][32 * RPL];   // broadcast tail x_j of the pivot column
+  float rowj[2][32];       // row j of the panel (CTA 0)
+  float dsum[2][32];       // per-column dot totals (single-CTA case)
+  float slot[2][64];       // cluster-visible partials: [column dots | pivot row]
+  float T[32][33];         // T factor (CTA 0)
+};
 
-  __shared__ float wsum[NW][NBT];
-  __shared__ float slot[2][2 * NBT];  // cluster-visible partials: [dots | row j]
-  __shared__ float tot_s[2][NBT];
-  __shared__ float rowj_s[2][NBT];
-  constexpr int TD = HAS_T ? NBT : 1;
-  __shared__ float T_s[TD][TD + 1];
+// Factor the panel whose column `warp` this warp holds in a[] (rows lane + 32 i of the
+// CTA's row block, p = cluster rank). All threads of the CTA -- and of the cluster when
+// cluster_size > 1 -- must call this with the same (w, jmax).
+template <int RPL, bool HAS_T>
+__device__ __forceinline__ void factor_panel_cols(float (&a)[RPL], const int w, const int jmax,
+                                                  PanelShared<RPL>& sh, float* __restrict__ tau_out,
+                                                  const int cluster_size, const int p) {
+  const int lane = threadIdx.x & 31, c = threadIdx.x >> 5;
+  const int lr0 = p * 32 * RPL + lane;  // local panel row of a[0]
+  cg::cluster_group cluster = cg::this_cluster();
 
+  for (int j = 0; j < jmax; ++j) {
+    const int ph = j & 1;
+    // (a) publish x_j and row j.
+    if (c == j) {
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) sh.xs[ph][lane + 32 * i] = (lr0 + 32 * i > j) ? a[i] : 0.f;
+    }
+    if (p == 0 && lane == j) sh.rowj[ph][c] = a[0];
+    __syncthreads();
+    // (c) d_c = x_j . a_c
+    float x[RPL];
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) {
+      x[i] = sh.xs[ph][lane + 32 * i];
+      d = fmaf(x[i], a[i], d);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) d += __shfl_xor_sync(kFullMask, d, o);
+    float xn2, alpha, ajc;
+    if (cluster_size == 1) {
+      if (lane == 0) sh.dsum[ph][c] = d;
+      __syncthreads();
+      xn2 = sh.dsum[ph][j];
+      alpha = sh.rowj[ph][j];
+      ajc = sh.rowj[ph][c];
+    } else {
+      if (lane == 0) {
+        sh.slot[ph][c] = d;
+        sh.slot[ph][32 + c] = (p == 0) ? sh.rowj[ph][c] : 0.f;
+      }
+      cluster.sync();
+      // Gather the CTA partials in one round: lane q < cluster_size reads CTA q's slot for this
+      // warp's column and for the pivot column, lane 0 of CTA 0's slot also holds the pivot row.
+      float dd = 0.f, xx = 0.f, pv = 0.f;
+      if (lane < cluster_size) {
+        const float* rq = cluster.map_shared_rank(&sh.slot[ph][0], lane);
+        dd = rq[c];
+        xx = rq[j];
+      } else if (lane == 8 || lane == 9) {  // pivot-row entries a[j][j] and a[j][c] from CTA 0
+        pv = cluster.map_shared_rank(&sh.slot[ph][0], 0)[32 + (lane == 8 ? j : c)];
+      }
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) {  // cluster_size <= 8
+        dd += __shfl_xor_sync(kFullMask, dd, o);
+        xx += __shfl_xor_sync(kFullMask, xx, o);
+      }
+      d = __shfl_sync(kFullMask, dd, 0);
+      xn2 = __shfl_sync(kFullMask, xx, 0);
+      alpha = __shfl_sync(kFullMask, pv, 8);
+      ajc = __shfl_sync(kFullMask, pv, 9);
+      if (HAS_T) {  // cluster totals for the T column built by warp j of CTA 0
+        if (lane == 0) sh.dsum[ph][c] = d;
+        __syncthreads();
+      }
+    }
+    // (d) reflector and updates.
+    const Reflector rf = make_reflector(alpha, xn2);
+    if (c > j && c < w) {
+      const float wc = fmaf(rf.scale, d, ajc);
+      const float cx = rf.tau * rf.scale * wc;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        const int lr = lr0 + 32 * i;
+        if (lr > j) a[i] = fmaf(-cx, x[i], a[i]);
+        else if (lr == j) a[i] = fmaf(-rf.tau, wc, a[i]);
+      }
+    } else if (c == j) {
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        const int lr = lr0 + 32 * i;
+        if (lr > j) a[i] *= rf.scale;
+        else if (lr == j) a[i] = rf.diag;
+      }
+      if (p == 0) {
+        if (lane == 0) tau_out[j] = rf.tau;
+        if (HAS_T) {
+          float acc = 0.f;
+          for (int cc = lane; cc < j; ++cc)
+            acc = fmaf(sh.T[lane][cc], fmaf(rf.scale, sh.dsum[ph][cc], sh.rowj[ph][cc]), acc);
+          if (lane < j) sh.T[lane][j] = -rf.tau * acc;
+          if (lane == j) sh.T[j][j] = rf.tau;
+        }
+      }
+    }
+  }
+}
+
+// Single-CTA panel, "owner computes" form: used when the whole panel fits one CTA.
+// NW = 32 / CPW warps; warp g owns columns g + NW q (q < CPW), interleaved so that the
+// still-active columns stay spread over all warps. Reflector j:
+//   the owner warp (j % NW) reduces ||x_j||^2 over its column, computes beta, tau and the
+//   scale once, scales its tail into v_j and publishes v_j (unit at row j, zero above) and
+//   tau in shared memory;  ONE __syncthreads;  every warp then forms v_j^T a_c for its
+//   active columns c > j (warp all-reduce) and applies a_c -= tau (v_j^T a_c) v_j, and for
+//   its finished columns c < j records G[c][j] = v_c^T v_j for the T factor.
+// T is assembled after the loop by the LARFT recurrence over G (one warp).
+template <int RPL, int CPW>
+struct OwnerShared {
+  float v[2][32 * RPL];
+  float tau[32];
+  float G[32][33];
+  float T[32][33];
+};
+
+template <int RPL, int CPW, bool HAS_T>
+__device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const int w, const int jmax,
+                                                   OwnerShared<RPL, CPW>& sh, float* __restrict__ tau_out) {
+  constexpr int NW = 32 / CPW;
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  for (int j = 0; j < jmax; ++j) {
+    const int ph = j & 1;
+    if (g == j % NW) {
+      const int oq = j / NW;
+      float x[RPL];
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        float t = a[0][i];
+#pragma unroll
+        for (int q = 1; q < CPW; ++q) t = (q == oq) ? a[q][i] : t;
+        x[i] = t;
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) s = (lane + 32 * i > j) ? fmaf(x[i], x[i], s) : s;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
+      const float alpha = __shfl_sync(kFullMask, x[0], j);
+      const Reflector rf = make_reflector(alpha, s);
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        const int lr = lane + 32 * i;
+        const float vi = (lr > j) ? x[i] * rf.scale : (lr == j ? 1.f : 0.f);
+        sh.v[ph][lr] = vi;
+        const float nx = (lr > j) ? vi : (lr == j ? rf.diag : x[i]);
+#pragma unroll
+        for (int q = 0; q < CPW; ++q)
+          if (q == oq) a[q][i] = nx;
+      }
+      if (lane == 0) {
+        sh.tau[j] = rf.tau;
+        tau_out[j] = rf.tau;
+      }
+    }
+    __syncthreads();
+    const float tj = sh.tau[j];
+    float v[RPL];
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) v[i] = sh.v[ph][lane + 32 * i];
+    float dq[CPW];
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) {
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) d = fmaf(v[i], a[q][i], d);
+      dq[q] = d;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int q = 0; q < CPW; ++q) dq[q] += __shfl_xor_sync(kFullMask, dq[q], o);
+#pragma unroll
+    for (int q = 0; q < CPW; ++q) {
+      const int c = g + NW * q;
+      if (c > j && c < w) {
+        const float f = tj * dq[q];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) a[q][i] = fmaf(-f, v[i], a[q][i]);
+      } else if (HAS_T && c < j) {
+        if (lane == 0) sh.G[c][j] = dq[q];
+      }
+    }
+  }
+  if (HAS_T) {
+    __syncthreads();
+    if (g == 0) {
+      // LARFT: T[i][j] = -tau_j sum_{i<=c<j} T[i][c] G[c][j], T[j][j] = tau_j (lane i = row).
+      for (int j = 0; j < jmax; ++j) {
+        float acc = 0.f;
+        for (int c = 0; c < j; ++c) {
+          const float t = sh.T[lane][c];
+          acc = (c >= lane) ? fmaf(t, sh.G[c][j], acc) : acc;
+        }
+        const float tj = sh.tau[j];
+        sh.T[lane][j] = (lane < j) ? -tj * acc : (lane == j ? tj : 0.f);
+        __syncwarp();
+      }
+    }
+  }
+}
+
+// Two CTAs per SM for the 8-warp shape (<= 128 registers), so one CTA's reflector latency
+// overlaps another matrix's panel.
+template <int RPL, int CPW, bool HAS_T>
+__global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_owner_kernel(PanelParams P) {
+  constexpr int NW = 32 / CPW;
+  __shared__ OwnerShared<RPL, CPW> sh;
+  const int bidx = blockIdx.y;
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int n = P.n, k = P.k, w = P.w;
+  const int m = n - k;
+  const float* __restrict__ S = P.src + (long long)bidx * P.src_bstride;
+  float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  if (HAS_T)
+    for (int i = threadIdx.x; i < 32 * 33; i += 32 * NW) (&sh.T[0][0])[i] = 0.f;
+  float a[CPW][RPL];
+#pragma unroll
+  for (int q = 0; q < CPW; ++q) {
+    const int c = g + NW * q;
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) {
+      const int lr = lane + 32 * i;
+      a[q][i] = (lr < m && c < w) ? S[(long long)(k + lr) * n + k + c] : 0.f;
+    }
+  }
+  __syncthreads();
+  factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
+#pragma unroll
+  for (int q = 0; q < CPW; ++q) {
+    const int c = g + NW * q;
+    if (c >= w) continue;
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) {
+      const int lr = lane + 32 * i;
+      if (lr < m) Hb[(long long)(k + lr) * n + k + c] = a[q][i];
+    }
+  }
+  if (HAS_T && P.T != nullptr) {
+    __syncthreads();
+    float* Tb = P.T + (long long)bidx * 32 * 32;
+    for (int i = threadIdx.x; i < 32 * 32; i += 32 * NW) Tb[i] = sh.T[i / 32][i % 32];
+  }
+}
+
+template <int RPL, bool HAS_T>
+__global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams P) {
+  constexpr int R = 32 * RPL;
+  __shared__ PanelShared<RPL> sh;
   cg::cluster_group cluster = cg::this_cluster();
   const int CP = (int)cluster.num_blocks();
   const int p = (int)cluster.block_rank();
   const int bidx = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lane = threadIdx.x & 31, c = threadIdx.x >> 5;
   const int n = P.n, k = P.k, w = P.w;
   const int m = n - k;
-  const bool want_T = HAS_T && P.T != nullptr;
   const float* __restrict__ S = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Hb = P.H + (long long)bidx * n * n;
 
-  for (int i = tid; i < TD * (TD + 1); i += NT) (&T_s[0][0])[i] = 0.f;
+  if (HAS_T)
+    for (int i = threadIdx.x; i < 32 * 33; i += kPanelThreads) (&sh.T[0][0])[i] = 0.f;
 
-  float a[RPT][NBT];
+  float a[RPL];
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const int lr = p * R + i * NT + tid;
-    if (lr < m) {
-      const float* row = S + (long long)(k + lr) * n + k;
-#pragma unroll
-      for (int c = 0; c < NBT; ++c) a[i][c] = (c < w) ? row[c] : 0.f;
-    } else {
-#pragma unroll
-      for (int c = 0; c < NBT; ++c) a[i][c] = 0.f;
-    }
+  for (int i = 0; i < RPL; ++i) {
+    const int lr = p * R + lane + 32 * i;
+    a[i] = (lr < m && c < w) ? S[(long long)(k + lr) * n + k + c] : 0.f;
   }
-  if (CP > 1) cluster.sync();  // every CTA of the cluster is running before any DSMEM access
+  if (CP > 1) cluster.sync();  // every CTA of the cluster runs before any DSMEM access
   __syncthreads();
 
-  const int jmax = min(w, m);
-  for (int j = 0; j < jmax; ++j) {
-    const int ph = j & 1;
-    float d[NBT];
-#pragma unroll
-    for (int c = 0; c < NBT; ++c) d[c] = 0.f;
-    float xj[RPT];
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const int lr = p * R + i * NT + tid;
-      float x = 0.f;
-#pragma unroll
-      for (int c = 0; c < NBT; ++c) x = (c == j) ? a[i][c] : x;
-      xj[i] = x;
-      const float f = (lr > j) ? x : 0.f;
-#pragma unroll
-      for (int c = 0; c < NBT; ++c) d[c] = fmaf(f, a[i][c], d[c]);
-      if (lr == j) {
-#pragma unroll
-        for (int c = 0; c < NBT; ++c) rowj_s[ph][c] = a[i][c];
-      }
-    }
-    warp_transpose_reduce<NBT>(d, lane);
-#pragma unroll
-    for (int q = 0; q < Q; ++q) wsum[warp][lane * Q + q] = d[q];
-    __syncthreads();
-    if (warp == 0) {
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        const int c = lane * Q + q;
-        float s = 0.f;
-#pragma unroll
-        for (int v = 0; v < NW; ++v) s += wsum[v][c];
-        if (CP == 1) {
-          tot_s[ph][c] = s;
-        } else {
-          slot[ph][c] = s;
-          slot[ph][NBT + c] = (p == 0) ? rowj_s[ph][c] : 0.f;
-        }
-      }
-    }
-    if (CP > 1) {
-      cluster.sync();
-      if (warp == 0) {
-        const float* r0 = cluster.map_shared_rank(&slot[ph][0], 0);
-#pragma unroll
-        for (int q = 0; q < Q; ++q) {
-          const int c = lane * Q + q;
-          float s = 0.f;
-          for (int qq = 0; qq < CP; ++qq) s += cluster.map_shared_rank(&slot[ph][0], qq)[c];
-          tot_s[ph][c] = s;
-          if (p != 0) rowj_s[ph][c] = r0[NBT + c];
-        }
-      }
-    }
-    __syncthreads();
+  factor_panel_cols<RPL, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k, CP, p);
 
-    const float alpha = rowj_s[ph][j];
-    const Reflector rf = make_reflector(alpha, tot_s[ph][j]);
-    // wv[c] = v_j^T a_c for the trailing panel columns (v_j = e_j + scale * x_j).
-    float wv[NBT];
+  if (c < w) {
 #pragma unroll
-    for (int c = 0; c < NBT; ++c) wv[c] = fmaf(rf.scale, tot_s[ph][c], rowj_s[ph][c]);
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const int lr = p * R + i * NT + tid;
-      if (lr >= j) {
-        const bool diag_row = (lr == j);
-        const float coef = diag_row ? rf.tau : rf.tau * rf.scale * xj[i];
-        const float newj = diag_row ? rf.diag : rf.scale * xj[i];
-#pragma unroll
-        for (int c = 0; c < NBT; ++c) {
-          if (c > j) a[i][c] = fmaf(-coef, wv[c], a[i][c]);
-          if (c == j) a[i][c] = newj;
-        }
-      }
-    }
-    if (p == 0) {
-      if (tid == 0) P.tau[(long long)bidx * n + k + j] = rf.tau;
-      if (HAS_T && want_T && warp == NW - 1) {
-        // T[i][j] = -tau_j * sum_{i <= c < j} T[i][c] * z_c ; T[j][j] = tau_j.
-        // z_c = v_c . v_j = a[j][c] + scale * d_c for c < j, which is wv[c].
-        for (int i = lane; i <= j; i += 32) {
-          float acc = 0.f;
-#pragma unroll
-          for (int c = 0; c < NBT; ++c)
-            if (c >= i && c < j) acc = fmaf(T_s[i % TD][c % TD], wv[c], acc);
-          T_s[i % TD][j % TD] = (i == j) ? rf.tau : -rf.tau * acc;
-        }
-      }
+    for (int i = 0; i < RPL; ++i) {
+      const int lr = p * R + lane + 32 * i;
+      if (lr < m) Hb[(long long)(k + lr) * n + k + c] = a[i];
     }
   }
-
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) {
-    const int lr = p * R + i * NT + tid;
-    if (lr < m) {
-      float* row = Hb + (long long)(k + lr) * n + k;
-#pragma unroll
-      for (int c = 0; c < NBT; ++c)
-        if (c < w) row[c] = a[i][c];
-    }
-  }
-  // Columns of a row that lies above the panel but inside the matrix are written by the
-  // previous panels' trailing updates; nothing else to store here.
-  if (HAS_T && want_T && p == 0) {
+  if (HAS_T && P.T != nullptr && p == 0) {
     __syncthreads();
-    float* Tb = P.T + (long long)bidx * NBT * NBT;
-    for (int i = tid; i < NBT * NBT; i += NT) Tb[i] = T_s[(i / NBT) % TD][(i % NBT) % TD];
+    float* Tb = P.T + (long long)bidx * 32 * 32;
+    for (int i = threadIdx.x; i < 32 * 32; i += kPanelThreads) Tb[i] = sh.T[i / 32][i % 32];
   }
   if (CP > 1) cluster.sync();  // keep this CTA's shared memory alive for remote readers
 }

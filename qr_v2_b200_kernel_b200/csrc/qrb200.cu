@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -16,28 +17,27 @@
 
 #include "../../include/qrb200.h"
 #include "panel.cuh"
+#include "small.cuh"
 #include "wy_simt.cuh"
+#include "wy_tc.cuh"
 
 namespace qrb200 {
 
 constexpr int kNB = 32;              // panel width of the blocked path
-constexpr int kPanelThreads = 256;   // threads per panel CTA
-constexpr int kPanelRPT = 2;         // panel rows per thread
-constexpr int kPanelRows = kPanelThreads * kPanelRPT;  // rows per panel CTA
+constexpr int kPanelRows = 512;      // panel rows per CTA of a cluster (32 lanes x 16 rows)
 constexpr int kMaxCluster = 8;       // portable cluster size
 constexpr int kMaxN = kPanelRows * kMaxCluster;        // 4096
-constexpr int kSmallN = 64;          // whole-matrix single-CTA path up to this order
+constexpr int kSmallN = 128;         // whole-matrix single-CTA path up to this order
 
-__device__ int g_device_status = 0;
 
 // ---------------------------------------------------------------------------------------
 // Launch accounting. Every kernel launch goes through LaunchScope, which counts it and,
 // while a profiling call is active on this host thread, brackets it with CUDA events and
 // records its algorithmic flops and bytes.
-enum KernelKind { K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_NUM_KINDS };
-static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc",
-                                                   "wy_tw", "wy_upd"};
-static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1};
+enum KernelKind { K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_TC_VTC, K_TC_UPD, K_NUM_KINDS };
+static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw",
+                                                   "wy_upd", "tc_vtc", "tc_upd"};
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1};
 
 static std::atomic<long long> g_launches{0};
 
@@ -78,19 +78,25 @@ static double panel_flops(double m, double w) { return 2.0 * m * w * w - 2.0 * w
 static inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
 static inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Row splits of the V^T C product for panel k: enough CTAs to cover the GPU twice.
-static int choose_nsplit(long long batch, int n, int k, int w) {
+// Row splits of the V^T C product for panel k. A function of the panel height only, so a
+// matrix's arithmetic (and therefore its result, bit for bit) does not depend on how many
+// other matrices share the call -- batch shards on several GPUs reproduce one GPU exactly.
+constexpr int kRowsPerSplit = 256;
+static int choose_nsplit(long long /*batch*/, int n, int k, int w) {
   const int m = n - k, nc = n - k - w;
   if (nc <= 0) return 1;
-  const long long tiles = (long long)cdiv(nc, 64) * batch;
-  int ns = (int)std::min<long long>(8, std::max<long long>(1, (296 + tiles - 1) / tiles));
-  ns = std::min(ns, std::max(1, m / 128));
-  return ns;
+  return std::max(1, cdiv(m, kRowsPerSplit));
 }
+
+static int choose_nsplit_tc(long long batch, int m, int nc);
 
 static int max_nsplit(long long batch, int n) {
   int mx = 1;
-  for (int k = 0; k < n; k += kNB) mx = std::max(mx, choose_nsplit(batch, n, k, std::min(kNB, n - k)));
+  for (int k = 0; k < n; k += kNB) {
+    const int w = std::min(kNB, n - k);
+    mx = std::max(mx, choose_nsplit(batch, n, k, w));
+    if (n - k - w > 0) mx = std::max(mx, choose_nsplit_tc(batch, n - k, n - k - w));
+  }
   return mx;
 }
 
@@ -127,11 +133,11 @@ static int check_device() {
   return cached;
 }
 
-template <int NBT, int NT, int RPT, bool HAS_T>
+template <int RPL, bool HAS_T>
 static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
-  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.blockDim = dim3(kPanelThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -141,17 +147,91 @@ static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long ba
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, panel_factor_kernel<NBT, NT, RPT, HAS_T>, pp);
+  return cudaLaunchKernelEx(&cfg, panel_factor_kernel<RPL, HAS_T>, pp);
 }
 
-// Whole-matrix factorisation by one CTA (n <= 64): the panel kernel with width n.
+template <int NMAX>
+static cudaError_t launch_small(const float* A, float* H, float* tau, long long batch, int n,
+                                long long abs, cudaStream_t s) {
+  const size_t smem = sizeof(SmallShared<NMAX>);
+  static bool configured = false;  // per instantiation; attribute is per device function
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(small_qr_kernel<NMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  small_qr_kernel<NMAX><<<(unsigned)batch, kPanelThreads, smem, s>>>(A, abs, H, tau, n);
+  return cudaGetLastError();
+}
+
+// Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch.
 static cudaError_t run_small(const float* A, float* H, float* tau, long long batch, int n,
                              long long abs, cudaStream_t s) {
-  PanelParams pp{A, abs, H, tau, nullptr, n, 0, n};
   LaunchScope ls(K_SMALL, batch * 4.0 * n * (double)n * n / 3.0, batch * 8.0 * n * (double)n);
-  if (n <= 32) return launch_panel<32, 32, 1, false>(pp, 1, batch, s);
-  return launch_panel<64, 64, 1, false>(pp, 1, batch, s);
+  if (n <= 64) return launch_small<64>(A, H, tau, batch, n, abs, s);
+  return launch_small<128>(A, H, tau, batch, n, abs, s);
 }
+
+template <int RPL, int CPW>
+static cudaError_t launch_owner(const PanelParams& pp, long long batch, cudaStream_t s) {
+  panel_owner_kernel<RPL, CPW, true><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), 0, s>>>(pp);
+  return cudaGetLastError();
+}
+
+static int panel_cpw() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_PANEL_CPW");
+    v = e ? atoi(e) : 4;
+    if (v != 1 && v != 2 && v != 4) v = 4;
+  }
+  return v;
+}
+
+template <int RPL>
+static cudaError_t launch_owner_cpw(const PanelParams& pp, long long batch, cudaStream_t s) {
+  switch (panel_cpw()) {
+    case 1: return launch_owner<RPL, 1>(pp, batch, s);
+    case 2: return launch_owner<RPL, 2>(pp, batch, s);
+    default: return launch_owner<RPL, 4>(pp, batch, s);
+  }
+}
+
+// Panel kernel shape by panel height: panels up to 512 rows are factored by one CTA
+// ("owner computes" form, rows spread over the lanes of each column's warp); taller panels
+// use a cluster of ceil(m / 512) CTAs of 32 warps (one per column).
+static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s) {
+  if (m <= 128) return launch_owner_cpw<4>(pp, batch, s);
+  if (m <= 256) return launch_owner_cpw<8>(pp, batch, s);
+  if (m <= 512) return launch_owner_cpw<16>(pp, batch, s);
+  return launch_panel<16, true>(pp, cdiv(m, kPanelRows), batch, s);
+}
+
+// Trailing-update implementation for 32-wide panels: CUDA cores (default: at this width the
+// update is bound by HBM traffic, which the FP32 kernels already stream at ~60 % of peak) or
+// the tensor-core kernels (QRB200_WY=tc; needs n % 4 == 0 and 16-byte aligned input).
+static bool use_tc_update(int n, const float* A, long long abs) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_WY");
+    v = (e && strcmp(e, "tc") == 0) ? 1 : 0;
+  }
+  return v == 1 && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+}
+
+static cudaError_t tc_configure() {
+  static bool done = false;
+  if (done) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(tc_vtc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtcSmem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(tc_upd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpdSmem);
+  if (e != cudaSuccess) return e;
+  done = true;
+  return cudaSuccess;
+}
+
+// Row splits of the tensor-core V^T C product (panel height only, see choose_nsplit).
+static int choose_nsplit_tc(long long /*batch*/, int m, int /*nc*/) { return std::max(1, cdiv(m, kRowsPerSplit)); }
 
 static cudaError_t run_blocked(const float* A, float* H, float* tau, long long batch, int n,
                                long long abs, const Workspace& ws, cudaStream_t s) {
@@ -162,15 +242,43 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     const int nc = n - k - w;
     const float* src = (k == 0) ? A : H;
     const long long sbs = (k == 0) ? abs : (long long)n * n;
-    const int cluster = cdiv(m, kPanelRows);
     PanelParams pp{src, sbs, H, tau, nc > 0 ? ws.T : nullptr, n, k, w};
     cudaError_t e;
     {
       LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
-      e = launch_panel<kNB, kPanelThreads, kPanelRPT, true>(pp, cluster, batch, s);
+      e = launch_panel_for(pp, m, batch, s);
     }
     if (e != cudaSuccess) return e;
     if (nc <= 0) continue;
+    if (use_tc_update(n, A, abs)) {
+      e = tc_configure();
+      if (e != cudaSuccess) return e;
+      WyParams wp{};
+      wp.src = src;
+      wp.src_bstride = sbs;
+      wp.H = H;
+      wp.T = ws.T;
+      wp.Wp = ws.Wp;
+      wp.n = n;
+      wp.k = k;
+      wp.w = w;
+      wp.nsplit = choose_nsplit_tc(batch, m, nc);
+      wp.rows_per_split = kRowsPerSplit;
+      wp.ncmax = ncmax;
+      const double bm = (double)batch * m;
+      {
+        LaunchScope ls(K_TC_VTC, 2.0 * bm * w * nc, 4.0 * bm * (w + nc) + 4.0 * batch * wp.nsplit * w * (double)nc);
+        tc_vtc_kernel<<<dim3(cdiv(nc, kTcCols), wp.nsplit, (unsigned)batch), 128, kVtcSmem, s>>>(wp);
+      }
+      {
+        LaunchScope ls(K_TC_UPD, 2.0 * bm * w * nc + (double)batch * w * w * nc,
+                       8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * wp.nsplit * w * (double)nc);
+        tc_upd_kernel<<<dim3(cdiv(nc, kTcCols), cdiv(m, kTcRows), (unsigned)batch), 128, kUpdSmem, s>>>(wp);
+      }
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      continue;
+    }
     WyParams wp{};
     wp.src = src;
     wp.src_bstride = sbs;
@@ -182,7 +290,7 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     wp.k = k;
     wp.w = w;
     wp.nsplit = choose_nsplit(batch, n, k, w);
-    wp.rows_per_split = cdiv(cdiv(m, wp.nsplit), 32) * 32;
+    wp.rows_per_split = kRowsPerSplit;
     wp.ncmax = ncmax;
     const double bm = (double)batch * m;
     {
