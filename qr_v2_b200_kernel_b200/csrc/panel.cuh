@@ -41,10 +41,11 @@ struct PanelParams {
   long long src_bstride;  // elements between matrices of src
   float* H;               // output batch, n x n row-major, contiguous
   float* tau;             // batch x n
-  float* T;               // batch x 32 x 32 upper-triangular T factors (may be null)
+  float* T;               // 32 x 32 upper-triangular T factors, t_bstride apart (may be null)
   int n;                  // matrix order
   int k;                  // first panel column (== first panel row)
   int w;                  // panel width, <= 32
+  long long t_bstride;    // elements between the T factors of consecutive matrices
 };
 
 template <int RPL>
@@ -296,7 +297,7 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_own
   }
   if (HAS_T && P.T != nullptr) {
     __syncthreads();
-    float* Tb = P.T + (long long)bidx * 32 * 32;
+    float* Tb = P.T + (long long)bidx * P.t_bstride;
     for (int i = threadIdx.x; i < 32 * 32; i += 32 * NW) Tb[i] = sh.T[i / 32][i % 32];
   }
 }
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams
   }
   if (HAS_T && P.T != nullptr && p == 0) {
     __syncthreads();
-    float* Tb = P.T + (long long)bidx * 32 * 32;
+    float* Tb = P.T + (long long)bidx * P.t_bstride;
     for (int i = threadIdx.x; i < 32 * 32; i += kPanelThreads) Tb[i] = sh.T[i / 32][i % 32];
   }
   if (CP > 1) cluster.sync();  // keep this CTA's shared memory alive for remote readers

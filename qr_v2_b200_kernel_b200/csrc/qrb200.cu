@@ -20,6 +20,7 @@
 #include "small.cuh"
 #include "wy_simt.cuh"
 #include "wy_tc.cuh"
+#include "wy_tc128.cuh"
 
 namespace qrb200 {
 
@@ -34,10 +35,14 @@ constexpr int kSmallN = 128;         // whole-matrix single-CTA path up to this 
 // Launch accounting. Every kernel launch goes through LaunchScope, which counts it and,
 // while a profiling call is active on this host thread, brackets it with CUDA events and
 // records its algorithmic flops and bytes.
-enum KernelKind { K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_TC_VTC, K_TC_UPD, K_NUM_KINDS };
-static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw",
-                                                   "wy_upd", "tc_vtc", "tc_upd"};
-static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1};
+enum KernelKind {
+  K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_TC_VTC, K_TC_UPD,
+  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_NUM_KINDS
+};
+static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw", "wy_upd",
+                                                   "tc_vtc", "tc_upd", "tc_gram", "tbuild", "tc_ygemm", "tc_vtc128",
+                                                   "tc_upd128"};
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1, 1, 0, 1, 1, 1};
 
 static std::atomic<long long> g_launches{0};
 
@@ -101,24 +106,48 @@ static int max_nsplit(long long batch, int n) {
 }
 
 struct Workspace {
-  float* T;
-  float* Wp;
-  float* W2;
+  float* T;     // single-level: batch x 32 x 32; two-level: panel factors batch x 4 x 32 x 32
+  float* Wp;    // single-level / narrow-update partials: batch x nsplit x 32 x ncmax
+  float* W2;    // batch x 32 x ncmax
+  float* Tob;   // two-level: batch x 128 x 128 outer-block factors
+  float* Gp;    // two-level: batch x nsplit_g x 128 x 128 Gram partials
+  float* Y;     // two-level: batch x n x 128  (V T^T)
+  float* Wf;    // two-level: batch x nsplit_f x n x 128 (W^T partials of the wide update)
   size_t bytes;
 };
 
+constexpr int kRowsPerSplitWide = 512;  // row split of the 128-wide products (panel height only)
+
+// Two-level (128-column outer blocks on the tensor cores) whenever the matrix is large enough
+// and its rows are 16-byte aligned; QRB200_TWO_LEVEL=0 selects the single-level path.
+static bool use_two_level(int n, const float* A, long long abs) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_TWO_LEVEL");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1 && n > kOB && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+}
+
 static Workspace layout(long long batch, int n, void* base) {
   Workspace ws{};
-  const size_t t_bytes = align_up((size_t)batch * kNB * kNB * sizeof(float), 256);
-  const size_t w_elems = (size_t)batch * kNB * (size_t)n;
+  auto carve = [&](size_t bytes) {
+    const size_t off = ws.bytes;
+    ws.bytes += align_up(bytes, 256);
+    return reinterpret_cast<float*>(static_cast<char*>(base) + off);
+  };
+  if (n <= kSmallN) return ws;
+  const size_t f = sizeof(float);
   const int ns = max_nsplit(batch, n);
-  const size_t wp_bytes = align_up(w_elems * ns * sizeof(float), 256);
-  const size_t w2_bytes = align_up(w_elems * sizeof(float), 256);
-  char* p = static_cast<char*>(base);
-  ws.T = reinterpret_cast<float*>(p);
-  ws.Wp = reinterpret_cast<float*>(p + t_bytes);
-  ws.W2 = reinterpret_cast<float*>(p + t_bytes + wp_bytes);
-  ws.bytes = (n <= kSmallN) ? 0 : t_bytes + wp_bytes + w2_bytes;
+  ws.T = carve((size_t)batch * 4 * kNB * kNB * f);
+  ws.Wp = carve((size_t)batch * ns * kNB * (size_t)n * f);
+  ws.W2 = carve((size_t)batch * kNB * (size_t)n * f);
+  // Wide-update buffers (sized for the largest n; unused on the single-level path).
+  const int nsw = cdiv(n, kRowsPerSplitWide);
+  ws.Tob = carve((size_t)batch * kOB * kOB * f);
+  ws.Gp = carve((size_t)batch * nsw * kOB * kOB * f);
+  ws.Y = carve((size_t)batch * n * kOB * f);
+  ws.Wf = carve((size_t)batch * nsw * (size_t)n * kOB * f);
   return ws;
 }
 
@@ -200,11 +229,13 @@ static cudaError_t launch_owner_cpw(const PanelParams& pp, long long batch, cuda
 // Panel kernel shape by panel height: panels up to 512 rows are factored by one CTA
 // ("owner computes" form, rows spread over the lanes of each column's warp); taller panels
 // use a cluster of ceil(m / 512) CTAs of 32 warps (one per column).
-static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s) {
-  if (m <= 128) return launch_owner_cpw<4>(pp, batch, s);
-  if (m <= 256) return launch_owner_cpw<8>(pp, batch, s);
-  if (m <= 512) return launch_owner_cpw<16>(pp, batch, s);
-  return launch_panel<16, true>(pp, cdiv(m, kPanelRows), batch, s);
+static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s, long long t_bstride) {
+  PanelParams q = pp;
+  q.t_bstride = t_bstride;
+  if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
+  if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
+  if (m <= 512) return launch_owner_cpw<16>(q, batch, s);
+  return launch_panel<16, true>(q, cdiv(m, kPanelRows), batch, s);
 }
 
 // Trailing-update implementation for 32-wide panels: CUDA cores (default: at this width the
@@ -246,7 +277,7 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     cudaError_t e;
     {
       LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
-      e = launch_panel_for(pp, m, batch, s);
+      e = launch_panel_for(pp, m, batch, s, kNB * kNB);
     }
     if (e != cudaSuccess) return e;
     if (nc <= 0) continue;
@@ -258,10 +289,12 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
       wp.src_bstride = sbs;
       wp.H = H;
       wp.T = ws.T;
+      wp.t_bstride = kNB * kNB;
       wp.Wp = ws.Wp;
       wp.n = n;
       wp.k = k;
       wp.w = w;
+      wp.cend = n;
       wp.nsplit = choose_nsplit_tc(batch, m, nc);
       wp.rows_per_split = kRowsPerSplit;
       wp.ncmax = ncmax;
@@ -284,11 +317,13 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     wp.src_bstride = sbs;
     wp.H = H;
     wp.T = ws.T;
+    wp.t_bstride = kNB * kNB;
     wp.Wp = ws.Wp;
     wp.W2 = ws.W2;
     wp.n = n;
     wp.k = k;
     wp.w = w;
+    wp.cend = n;
     wp.nsplit = choose_nsplit(batch, n, k, w);
     wp.rows_per_split = kRowsPerSplit;
     wp.ncmax = ncmax;
@@ -304,6 +339,154 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     {
       LaunchScope ls(K_UPD, 2.0 * bm * w * nc, 8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * w * (double)nc);
       wy_upd_kernel<kNB><<<dim3(cdiv(nc, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+
+static cudaError_t tc128_configure() {
+  static bool done = false;
+  if (done) return cudaSuccess;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_Y>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_UPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
+  done = true;
+  return cudaSuccess;
+}
+
+// Narrow update inside an outer block: columns [k + w, cend) by the panel at k (FP32 cores).
+static cudaError_t launch_narrow(const float* src, long long sbs, float* H, const float* T, const Workspace& ws,
+                                 long long batch, int n, int k, int w, int cend, cudaStream_t s) {
+  const int m = n - k, nc = cend - k - w;
+  WyParams wp{};
+  wp.src = src;
+  wp.src_bstride = sbs;
+  wp.H = H;
+  wp.T = T;
+  wp.t_bstride = 4 * kNB * kNB;
+  wp.Wp = ws.Wp;
+  wp.W2 = ws.W2;
+  wp.n = n;
+  wp.k = k;
+  wp.w = w;
+  wp.cend = cend;
+  wp.nsplit = choose_nsplit(batch, n, k, w);
+  wp.rows_per_split = kRowsPerSplit;
+  wp.ncmax = n;
+  const double bm = (double)batch * m;
+  {
+    LaunchScope ls(K_VTC, 2.0 * bm * w * nc, 4.0 * bm * (w + nc) + 4.0 * batch * wp.nsplit * w * (double)nc);
+    wy_vtc_kernel<kNB><<<dim3(cdiv(nc, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
+  }
+  {
+    LaunchScope ls(K_TW, (double)batch * w * w * nc, 4.0 * batch * (wp.nsplit + 1.0) * w * nc);
+    wy_tw_kernel<kNB><<<dim3(cdiv(nc, 128), (unsigned)batch), 128, 0, s>>>(wp);
+  }
+  {
+    LaunchScope ls(K_UPD, 2.0 * bm * w * nc, 8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * w * (double)nc);
+    wy_upd_kernel<kNB><<<dim3(cdiv(nc, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
+  }
+  return cudaGetLastError();
+}
+
+// Two-level blocked QR: outer blocks of 128 columns, each factored as four 32-column panels
+// with narrow updates inside the block, then one 128-wide tensor-core update of the trailing
+// matrix, C <- C - Y (V^T C) with Y = V T^T (T assembled from the block Gram matrix).
+static cudaError_t run_two_level(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                 const Workspace& ws, cudaStream_t s) {
+  cudaError_t e = tc128_configure();
+  if (e != cudaSuccess) return e;
+  for (int k0 = 0; k0 < n; k0 += kOB) {
+    const int ow = std::min(kOB, n - k0);
+    for (int kb = k0; kb < k0 + ow; kb += kNB) {
+      const int w = std::min(kNB, n - kb), m = n - kb;
+      const float* src = (kb == 0) ? A : H;
+      const long long sbs = (kb == 0) ? abs : (long long)n * n;
+      float* Tslot = ws.T + (size_t)((kb - k0) / kNB) * kNB * kNB;
+      // panel factors land in slot b of the batch x 4 x 32 x 32 array
+      PanelParams pp{src, sbs, H, tau, Tslot, n, kb, w};
+      {
+        LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+        e = launch_panel_for(pp, m, batch, s, 4 * kNB * kNB);
+      }
+      if (e != cudaSuccess) return e;
+      if (kb + w < k0 + ow) {
+        e = launch_narrow(src, sbs, H, Tslot, ws, batch, n, kb, w, k0 + ow, s);
+        if (e != cudaSuccess) return e;
+      }
+    }
+    if (k0 + ow >= n) break;
+    const int m = n - k0, nc = n - k0 - ow;
+    const float* src = (k0 == 0) ? A : H;
+    const long long sbs = (k0 == 0) ? abs : (long long)n * n;
+    const int nsw = cdiv(m, kRowsPerSplitWide);
+    const double bm = (double)batch * m;
+    // Gram matrix of the outer block's reflectors.
+    WyParams g{};
+    g.src = H;
+    g.src_bstride = (long long)n * n;
+    g.H = H;
+    g.Wp = ws.Gp;
+    g.n = n;
+    g.k = k0;
+    g.w = ow;
+    g.cend = n;
+    g.nsplit = nsw;
+    g.rows_per_split = kRowsPerSplitWide;
+    g.ncmax = kOB;
+    {
+      LaunchScope ls(K_GRAM, 2.0 * bm * ow * ow, 4.0 * bm * ow);
+      tc_vtcw_kernel<kOB, true><<<dim3(1, nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(g);
+    }
+    {
+      TbuildParams tp{ws.Gp, nsw, ws.T, ws.Tob, ow};
+      LaunchScope ls(K_TBUILD, batch * 2.0 * ow * ow * ow / 3.0, 4.0 * batch * (nsw + 1.0) * ow * ow);
+      tbuild_kernel<<<(unsigned)batch, 256, kTbuildSmem, s>>>(tp);
+    }
+    Gemm128Params gp{};
+    gp.H = H;
+    gp.src = src;
+    gp.src_bstride = sbs;
+    gp.Hout = H;
+    gp.T = ws.Tob;
+    gp.Y = ws.Y;
+    gp.y_bstride = (long long)n * kOB;
+    gp.Wp = ws.Wf;
+    gp.nsplit = nsw;
+    gp.ncmax = n;
+    gp.n = n;
+    gp.k = k0;
+    gp.w = ow;
+    gp.cend = n;
+    {
+      LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
+      tc_gemm128_kernel<MODE_Y><<<dim3(1, cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
+    }
+    WyParams wp{};
+    wp.src = src;
+    wp.src_bstride = sbs;
+    wp.H = H;
+    wp.Wp = ws.Wf;
+    wp.n = n;
+    wp.k = k0;
+    wp.w = ow;
+    wp.cend = n;
+    wp.nsplit = nsw;
+    wp.rows_per_split = kRowsPerSplitWide;
+    wp.ncmax = n;
+    {
+      LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
+      tc_vtcw_kernel<kOB, false><<<dim3(cdiv(nc, kTcCols), nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(wp);
+    }
+    {
+      LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
+      tc_gemm128_kernel<MODE_UPD><<<dim3(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -385,7 +568,8 @@ static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64
     const Workspace ws = layout(batch, (int)n, workspace);
     if (workspace_bytes < ws.bytes || !workspace) return QRB200_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return QRB200_ERR_WORKSPACE;
-    e = run_blocked(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
+    e = use_two_level((int)n, A, a_batch_stride) ? run_two_level(A, H, tau, batch, (int)n, a_batch_stride, ws, s)
+                                                   : run_blocked(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
   }
   if (e != cudaSuccess) return QRB200_ERR_CUDA;
   return QRB200_OK;

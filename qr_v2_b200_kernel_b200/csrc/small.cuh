@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kPanelThreads) small_qr_kernel(const float* __
   constexpr int NT = kPanelThreads;
   constexpr int RPL = NMAX / 32;
   constexpr int LD = SmallShared<NMAX>::LD;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   SmallShared<NMAX>& sh = *reinterpret_cast<SmallShared<NMAX>*>(smem_raw);
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;

@@ -19,13 +19,15 @@ struct WyParams {
   const float* src;       // trailing-matrix source (A for the first panel, else H)
   long long src_bstride;  // elements between matrices of src
   float* H;               // output batch (n x n row-major, contiguous)
-  const float* T;         // batch x NB x NB
-  float* Wp;              // batch x nsplit x NB x ncmax partial products
-  float* W2;              // batch x NB x ncmax
-  int n, k, w;            // panel start and width
+  const float* T;         // T factors, t_bstride elements apart (w x w, row stride w)
+  long long t_bstride;
+  float* Wp;              // partial products V^T C of the row splits
+  float* W2;              // T^T V^T C
+  int n, k, w;            // block reflector: rows/columns start at k, width w
+  int cend;               // trailing columns updated: [k + w, cend)
   int nsplit;             // row splits of the V^T C product
   int rows_per_split;     // multiple of 32
-  int ncmax;              // leading dimension of Wp / W2 rows (>= n - k - w)
+  int ncmax;              // leading dimension of Wp / W2 (>= cend - k - w)
 };
 
 // V[r][c] of the panel starting at (k, k): unit lower trapezoid stored in H.
@@ -42,7 +44,7 @@ __global__ void __launch_bounds__(256) wy_vtc_kernel(WyParams P) {
   __shared__ float Vs[32][NB + 1];
   __shared__ float Cs[32][64 + 1];
   const int bidx = blockIdx.z, split = blockIdx.y;
-  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = n - k - w;
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
   const int col0 = blockIdx.x * 64;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
@@ -84,8 +86,8 @@ template <int NB>
 __global__ void __launch_bounds__(128) wy_tw_kernel(WyParams P) {
   __shared__ float Ts[NB][NB + 1];
   const int bidx = blockIdx.y;
-  const int nc = P.n - P.k - P.w;
-  const float* Tb = P.T + (long long)bidx * NB * NB;
+  const int nc = P.cend - P.k - P.w;
+  const float* Tb = P.T + (long long)bidx * P.t_bstride;
   for (int e = threadIdx.x; e < NB * NB; e += blockDim.x) Ts[e / NB][e % NB] = Tb[e];
   __syncthreads();
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
@@ -114,7 +116,7 @@ __global__ void __launch_bounds__(256) wy_upd_kernel(WyParams P) {
   __shared__ float Vt[NB][64 + 4];  // V transposed: Vt[c][r]
   __shared__ float Ws[NB][64 + 4];
   const int bidx = blockIdx.z;
-  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = n - k - w;
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
   const int row0 = blockIdx.y * 64, col0 = blockIdx.x * 64;
   const float* __restrict__ Hb_in = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;

@@ -48,7 +48,7 @@ __device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
 }
 
 __global__ void __launch_bounds__(128) tc_vtc_kernel(WyParams P) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   VtcShared& sh = *reinterpret_cast<VtcShared*>(align1024(smem_raw));
   constexpr uint32_t LBO = 512, SBO_C = 2048, SBO_V = 512;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -168,7 +168,7 @@ struct UpdShared {
 constexpr size_t kUpdSmem = sizeof(UpdShared) + 1024;
 
 __global__ void __launch_bounds__(128) tc_upd_kernel(WyParams P) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   UpdShared& sh = *reinterpret_cast<UpdShared*>(align1024(smem_raw));
   constexpr uint32_t RS = 1024, CS = 128;
   const int tid = threadIdx.x, warp = tid >> 5;

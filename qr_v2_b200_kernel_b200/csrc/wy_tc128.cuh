@@ -1,0 +1,384 @@
+// Tensor-core pieces of the two-level blocked update (outer blocks of 128 columns made of
+// four 32-column panels). With V the 128 reflectors of an outer block (unit lower
+// trapezoid in H) and T its 128 x 128 compact-WY factor, the trailing columns C get
+//     C <- C - Y (V^T C),   Y = V T^T,
+// the same product as C - V T^T V^T C (milestones/01_eager_official123203us.py:102-107) with
+// the factor folded into V once per outer block:
+//
+//   tc_vtcw_kernel<128, false> : Wp[s]^T = C_s^T V_s  (row split s, MN-major SW128_32B operands)
+//   tc_vtcw_kernel<128, true>  : Gp[s]   = V_s^T V_s  (Gram of the outer block, same tile as A and B)
+//   tbuild_kernel               : T from the Gram and the four 32 x 32 panel factors
+//   tc_gemm128_kernel<Y>        : Y = V T^T            (128-row tiles, K = 128)
+//   tc_gemm128_kernel<UPD>      : C -= Y (sum_s Wp[s]) (128 x 128 tiles, K = 128)
+//
+// All products are 3xTF32 tcgen05 MMAs with FP32 accumulation in TMEM.
+#pragma once
+
+#include "tc.cuh"
+#include "wy_simt.cuh"
+#include "wy_tc.cuh"
+
+namespace qrb200 {
+
+constexpr int kOB = 128;  // outer block width (reflectors per fat update)
+
+// ---------------------------------------------------------------------------------------
+// W^T = C^T V (or G = V^T V) over one row split; M = 128 trailing columns (or V columns),
+// N = W, K = rows in 32-row stages.
+template <int W>
+struct VtcwStage {
+  float c_hi[kTcChunk * kTcCols];
+  float c_lo[kTcChunk * kTcCols];
+  float v_hi[kTcChunk * W];
+  float v_lo[kTcChunk * W];
+};
+template <int W>
+struct VtcwShared {
+  VtcwStage<W> st[2];
+  uint64_t mbar[2];
+  uint32_t tmem;
+};
+template <int W>
+constexpr size_t vtcw_smem() { return sizeof(VtcwShared<W>) + 1024; }
+
+template <int W, bool GRAM>
+__global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VtcwShared<W>& sh = *reinterpret_cast<VtcwShared<W>*>(align1024(smem_raw));
+  constexpr uint32_t LBO = 512, SBO_C = (kTcCols / 32) * 512, SBO_V = (W / 32) * 512;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, m = n - k;
+  const int nc = GRAM ? w : P.cend - k - w;
+  const int col0 = blockIdx.x * kTcCols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(m, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kTcChunk - 1) / kTcChunk : 0;
+
+  if (tid == 0) {
+    mbar_init(&sh.mbar[0], 1);
+    mbar_init(&sh.mbar[1], 1);
+    fence_async_smem();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem, W);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+  constexpr uint32_t idesc = make_idesc_tf32(128, W, true, true);
+  bool ok = true;
+  const int q8 = lane & 7, kr = lane >> 3;
+
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int s = ch & 1;
+    VtcwStage<W>& st = sh.st[s];
+    if (ch >= 2) ok = mbar_wait(&sh.mbar[s], ((ch >> 1) - 1) & 1) && ok;
+    const int r0 = r_begin + ch * kTcChunk;
+    // V chunk: W/32 x 8 atoms of the unit lower trapezoid (columns >= w are zero).
+#pragma unroll
+    for (int it = 0; it < W / 16; ++it) {
+      const int atom = it * 4 + warp;
+      const int c = (atom % (W / 32)) * 32 + 4 * q8, kk = (atom / (W / 32)) * 4 + kr;
+      const int r = r0 + kk;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < r_end && c < w) {
+        const float4 h = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
+        x.x = (r > c) ? h.x : (r == c ? 1.f : 0.f);
+        x.y = (c + 1 >= w) ? 0.f : ((r > c + 1) ? h.y : (r == c + 1 ? 1.f : 0.f));
+        x.z = (c + 2 >= w) ? 0.f : ((r > c + 2) ? h.z : (r == c + 2 ? 1.f : 0.f));
+        x.w = (c + 3 >= w) ? 0.f : ((r > c + 3) ? h.w : (r == c + 3 ? 1.f : 0.f));
+      }
+      float4 hi, lo;
+      split4(x, hi, lo);
+      const uint32_t off = sw32_off(c, kk, LBO, SBO_V) >> 2;
+      *reinterpret_cast<float4*>(st.v_hi + off) = hi;
+      *reinterpret_cast<float4*>(st.v_lo + off) = lo;
+    }
+    if (!GRAM) {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int atom = it * 4 + warp;
+        const int mn = (atom & 3) * 32 + 4 * q8, kk = (atom >> 2) * 4 + kr;
+        const int r = r0 + kk, col = col0 + mn;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < r_end && col < nc) x = *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + col);
+        float4 hi, lo;
+        split4(x, hi, lo);
+        const uint32_t off = sw32_off(mn, kk, LBO, SBO_C) >> 2;
+        *reinterpret_cast<float4*>(st.c_hi + off) = hi;
+        *reinterpret_cast<float4*>(st.c_lo + off) = lo;
+      }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      // Gram mode uses the V tile as A as well (M = W = 128 columns of V).
+      const uint32_t ach = smem_u32(GRAM ? st.v_hi : st.c_hi), acl = smem_u32(GRAM ? st.v_lo : st.c_lo);
+      const uint32_t sbo_a = GRAM ? SBO_V : SBO_C;
+      const uint32_t bvh = smem_u32(st.v_hi), bvl = smem_u32(st.v_lo);
+#pragma unroll
+      for (int ks = 0; ks < kTcChunk / 8; ++ks) {
+        mma_tf32x3(tmem, make_sdesc_sw32(ach + ks * 2 * sbo_a, LBO, sbo_a), make_sdesc_sw32(acl + ks * 2 * sbo_a, LBO, sbo_a),
+                   make_sdesc_sw32(bvh + ks * 2 * SBO_V, LBO, SBO_V), make_sdesc_sw32(bvl + ks * 2 * SBO_V, LBO, SBO_V),
+                   idesc, ch > 0 || ks > 0);
+      }
+      mma_commit(&sh.mbar[s]);
+    }
+  }
+  if (nchunks > 0) {
+    const int last = nchunks - 1;
+    ok = mbar_wait(&sh.mbar[last & 1], (last >> 1) & 1) && ok;
+  }
+  tc_fence_after();
+  // Epilogue: thread t owns row col0 + t of the result (W^T or G), W values.
+  const int col = col0 + tid;
+  float* out = P.Wp + (((long long)bidx * P.nsplit + split) * P.ncmax + col) * W;
+#pragma unroll 1
+  for (int q = 0; q < W / 32; ++q) {
+    float wv[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, wv);
+    if (nchunks == 0 || !ok) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) wv[i] = 0.f;
+    }
+    if (col < (GRAM ? W : nc)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(out + q * 32 + i) = make_float4(wv[i], wv[i + 1], wv[i + 2], wv[i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, W);
+}
+
+// ---------------------------------------------------------------------------------------
+// T of the outer block from its Gram matrix and the four 32 x 32 panel factors:
+//   T[0:32b, 32b:32b+32] = -T[0:32b, 0:32b] (G[0:32b, 32b:32b+32] T_b),   b = 1, 2, 3
+// (the block form of the LARFT recurrence of submission.py:129-137). One CTA per matrix.
+struct TbuildParams {
+  const float* Gp;        // batch x nsplit x 128 x 128 Gram partials
+  int nsplit;
+  const float* Tin;       // batch x 4 x 32 x 32 panel factors
+  float* Tout;            // batch x 128 x 128
+  int ow;                 // outer block width (multiple of 32, <= 128)
+};
+struct TbuildShared {
+  float G[kOB][kOB + 1];
+  float T[kOB][kOB + 1];
+  float X[96][33];
+};
+constexpr size_t kTbuildSmem = sizeof(TbuildShared);
+
+__global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  TbuildShared& sh = *reinterpret_cast<TbuildShared*>(smem_raw);
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int ow = P.ow;
+  for (int e = tid; e < kOB * kOB; e += 256) {
+    const int i = e / kOB, j = e % kOB;
+    float s = 0.f;
+    for (int q = 0; q < P.nsplit; ++q) s += P.Gp[(((long long)b * P.nsplit + q) * kOB + i) * kOB + j];
+    sh.G[i][j] = s;
+    sh.T[i][j] = 0.f;
+  }
+  __syncthreads();  // the zero fill must land before the diagonal blocks are written
+  for (int e = tid; e < 4 * 32 * 32; e += 256) {
+    const int blk = e / 1024, i = (e / 32) % 32, j = e % 32;
+    if (32 * blk < ow) sh.T[32 * blk + i][32 * blk + j] = P.Tin[(long long)b * 4096 + e];
+  }
+  __syncthreads();
+  for (int bb = 1; bb * 32 < ow; ++bb) {
+    const int r = 32 * bb;  // rows of the new column block
+    // X = G[0:r, r:r+32] T_bb
+    for (int e = tid; e < r * 32; e += 256) {
+      const int i = e / 32, j = e % 32;
+      float s = 0.f;
+#pragma unroll 8
+      for (int c = 0; c <= j; ++c) s = fmaf(sh.G[i][r + c], sh.T[r + c][r + j], s);
+      sh.X[i][j] = s;
+    }
+    __syncthreads();
+    // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r,0:r] upper triangular)
+    for (int e = tid; e < r * 32; e += 256) {
+      const int i = e / 32, j = e % 32;
+      float s = 0.f;
+      for (int c = i; c < r; ++c) s = fmaf(sh.T[i][c], sh.X[c][j], s);
+      sh.T[i][r + j] = -s;
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < kOB * kOB; e += 256) P.Tout[(long long)b * kOB * kOB + e] = sh.T[e / kOB][e % kOB];
+}
+
+// ---------------------------------------------------------------------------------------
+// 128 x 128 x 128 3xTF32 GEMM tile, K = 128 in four 32-wide double-buffered stages, both
+// operands K-major (no swizzle).
+//   MODE_Y  : P = V T^T  -> Y rows   (A = V rows of H, unit lower; B rows = T rows)
+//   MODE_UPD: P = Y W    -> C -= P   (A = Y rows; B rows = trailing columns, sum of the
+//                                     row-split partials W^T[col][0:128])
+enum Gemm128Mode { MODE_Y = 0, MODE_UPD = 1 };
+
+struct Gemm128Params {
+  const float* H;         // matrices (V source for MODE_Y; C destination for MODE_UPD)
+  const float* src;       // C source for MODE_UPD (A for the first outer block, else H)
+  long long src_bstride;
+  float* Hout;
+  const float* T;         // batch x 128 x 128 (MODE_Y)
+  float* Y;               // batch x ldy x 128 (row r of the outer block at r * 128)
+  long long y_bstride;
+  const float* Wp;        // batch x nsplit x ncmax x 128 (MODE_UPD)
+  int nsplit, ncmax;
+  int n, k, w;            // outer block: rows/columns from k, width w (<= 128)
+  int cend;               // MODE_UPD: trailing columns [k + w, cend)
+};
+
+struct Gemm128Stage {
+  float a_hi[128 * 32];
+  float a_lo[128 * 32];
+  float b_hi[128 * 32];
+  float b_lo[128 * 32];
+};
+struct Gemm128Shared {
+  Gemm128Stage st[2];
+  uint64_t mbar[2];
+  uint64_t done;
+  uint32_t tmem;
+};
+constexpr size_t kGemm128Smem = sizeof(Gemm128Shared) + 1024;
+
+template <int MODE>
+__global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Gemm128Shared& sh = *reinterpret_cast<Gemm128Shared*>(align1024(smem_raw));
+  constexpr uint32_t RS = 1024, CS = 128;  // 32-wide K chunk: 8 column quads per 8-row group
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bidx = blockIdx.z;
+  const int n = P.n, k = P.k, w = P.w, m = n - k;
+  const int ncols = (MODE == MODE_Y) ? kOB : P.cend - k - w;  // B rows (N extent)
+  const int col0 = blockIdx.x * 128, row0 = blockIdx.y * 128;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
+
+  if (tid == 0) {
+    mbar_init(&sh.mbar[0], 1);
+    mbar_init(&sh.mbar[1], 1);
+    mbar_init(&sh.done, 1);
+    fence_async_smem();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+  constexpr uint32_t idesc = make_idesc_tf32(128, 128, false, false);
+  bool ok = true;
+
+  for (int kc = 0; kc < 4; ++kc) {
+    const int s = kc & 1;
+    Gemm128Stage& st = sh.st[s];
+    if (kc >= 2) ok = mbar_wait(&sh.mbar[s], 0) && ok;
+    // A tile: 128 rows x 32 K (columns 32 kc .. 32 kc + 31 of V or Y).
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = it * 128 + tid;
+      const int rr = (idx & 7) + 8 * (idx >> 6);
+      const int cq = (idx >> 3) & 7;
+      const int r = row0 + rr, c = 32 * kc + 4 * cq;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < m && c < w) {
+        if (MODE == MODE_Y) {
+          const float4 h = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
+          x.x = (r > c) ? h.x : (r == c ? 1.f : 0.f);
+          x.y = (c + 1 >= w) ? 0.f : ((r > c + 1) ? h.y : (r == c + 1 ? 1.f : 0.f));
+          x.z = (c + 2 >= w) ? 0.f : ((r > c + 2) ? h.z : (r == c + 2 ? 1.f : 0.f));
+          x.w = (c + 3 >= w) ? 0.f : ((r > c + 3) ? h.w : (r == c + 3 ? 1.f : 0.f));
+        } else {
+          x = *reinterpret_cast<const float4*>(Yb + (long long)r * kOB + c);
+        }
+      }
+      float4 hi, lo;
+      split4(x, hi, lo);
+      const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
+      *reinterpret_cast<float4*>(st.a_hi + off) = hi;
+      *reinterpret_cast<float4*>(st.a_lo + off) = lo;
+    }
+    // B tile: 128 rows (N) x 32 K.
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int idx = it * 128 + tid;
+      const int rr = (idx & 7) + 8 * (idx >> 6);
+      const int cq = (idx >> 3) & 7;
+      const int j = col0 + rr, c = 32 * kc + 4 * cq;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < ncols && c < w) {
+        if (MODE == MODE_Y) {
+          x = *reinterpret_cast<const float4*>(P.T + ((long long)bidx * kOB + j) * kOB + c);
+        } else {
+          for (int q = 0; q < P.nsplit; ++q) {
+            const float4 t = *reinterpret_cast<const float4*>(
+                P.Wp + (((long long)bidx * P.nsplit + q) * P.ncmax + j) * kOB + c);
+            x.x += t.x; x.y += t.y; x.z += t.z; x.w += t.w;
+          }
+        }
+      }
+      float4 hi, lo;
+      split4(x, hi, lo);
+      const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
+      *reinterpret_cast<float4*>(st.b_hi + off) = hi;
+      *reinterpret_cast<float4*>(st.b_lo + off) = lo;
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ah = smem_u32(st.a_hi), al = smem_u32(st.a_lo);
+      const uint32_t bh = smem_u32(st.b_hi), bl = smem_u32(st.b_lo);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma_tf32x3(tmem, make_sdesc(ah + ks * 2 * CS, CS, RS), make_sdesc(al + ks * 2 * CS, CS, RS),
+                   make_sdesc(bh + ks * 2 * CS, CS, RS), make_sdesc(bl + ks * 2 * CS, CS, RS), idesc,
+                   kc > 0 || ks > 0);
+      // Stages 0 and 1 are refilled once (chunks 2 and 3): their first MMA batches signal
+      // mbar[s]; the last batch signals `done`, whose single phase covers every MMA issued.
+      if (kc < 2) mma_commit(&sh.mbar[s]);
+      if (kc == 3) mma_commit(&sh.done);
+    }
+  }
+  ok = mbar_wait(&sh.done, 0) && ok;
+  tc_fence_after();
+  // Epilogue: thread t owns tile row t (TMEM lane t).
+  const int r = row0 + tid;
+#pragma unroll 1
+  for (int q = 0; q < 4; ++q) {
+    float pv[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, pv);
+    if (!ok || r >= m) continue;
+    const int cbase = col0 + q * 32;
+    if (MODE == MODE_Y) {
+      float* yrow = P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + cbase;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(yrow + e) = make_float4(pv[e], pv[e + 1], pv[e + 2], pv[e + 3]);
+    } else {
+      const long long off = (long long)(k + r) * n + k + w + cbase;
+      const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+      float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        if (cbase + e < ncols) {
+          const float4 c = *reinterpret_cast<const float4*>(Sb + off + e);
+          *reinterpret_cast<float4*>(Ho + off + e) =
+              make_float4(c.x - pv[e], c.y - pv[e + 1], c.z - pv[e + 2], c.w - pv[e + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+}  // namespace qrb200
