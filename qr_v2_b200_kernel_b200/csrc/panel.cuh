@@ -48,14 +48,83 @@ struct PanelParams {
   long long t_bstride;    // elements between the T factors of consecutive matrices
 };
 
+// Coalesced panel transfer through shared memory. The panel rows [r0, r0 + rows) x columns
+// [k, k + w) of a row-major matrix are moved with 16-byte row segments and kept transposed in
+// `stage` (stage[c * ld + r], ld = rows + 1, so both the transposing writes and the per-column
+// reads are bank-conflict free); each warp then takes its columns from shared memory instead
+// of issuing one 4-byte load per row.
+__device__ __forceinline__ void panel_stage_in(const float* __restrict__ S, int n, int k, int r0, int rows,
+                                               int rows_valid, int w, float* stage, int nthreads) {
+  const int ld = rows + 1;
+  const bool vec = ((n & 3) == 0) && ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(S) & 15u) == 0);
+  for (int idx = threadIdx.x; idx < rows * 8; idx += nthreads) {
+    const int r = idx >> 3, q = idx & 7, c = 4 * q;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < rows_valid && c < w) {
+      const float* src = S + (long long)(k + r0 + r) * n + k + c;
+      if (vec && c + 3 < w) {
+        x = *reinterpret_cast<const float4*>(src);
+      } else {
+        x.x = src[0];
+        x.y = (c + 1 < w) ? src[1] : 0.f;
+        x.z = (c + 2 < w) ? src[2] : 0.f;
+        x.w = (c + 3 < w) ? src[3] : 0.f;
+      }
+    }
+    stage[(c + 0) * ld + r] = x.x;
+    stage[(c + 1) * ld + r] = x.y;
+    stage[(c + 2) * ld + r] = x.z;
+    stage[(c + 3) * ld + r] = x.w;
+  }
+}
+__device__ __forceinline__ void panel_stage_out(float* __restrict__ Hb, int n, int k, int r0, int rows,
+                                                int rows_valid, int w, const float* stage, int nthreads) {
+  const int ld = rows + 1;
+  const bool vec = ((n & 3) == 0) && ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(Hb) & 15u) == 0);
+  for (int idx = threadIdx.x; idx < rows * 8; idx += nthreads) {
+    const int r = idx >> 3, q = idx & 7, c = 4 * q;
+    if (r >= rows_valid || c >= w) continue;
+    const float4 x = make_float4(stage[(c + 0) * ld + r], stage[(c + 1) * ld + r], stage[(c + 2) * ld + r],
+                                 stage[(c + 3) * ld + r]);
+    float* dst = Hb + (long long)(k + r0 + r) * n + k + c;
+    if (vec && c + 3 < w) {
+      *reinterpret_cast<float4*>(dst) = x;
+    } else {
+      dst[0] = x.x;
+      if (c + 1 < w) dst[1] = x.y;
+      if (c + 2 < w) dst[2] = x.z;
+      if (c + 3 < w) dst[3] = x.w;
+    }
+  }
+}
+
 template <int RPL>
 struct PanelShared {
-  float xs[2][32 * RPL];   // broadcast tail x_j of the pivot column
-  float rowj[2][32];       // row j of the panel (CTA 0)
-  float dsum[2][32];       // per-column dot totals (single-CTA case)
-  float slot[2][64];       // cluster-visible partials: [column dots | pivot row]
+  float xs[2][32 * RPL];                // broadcast tail x_j of the pivot column
+  __align__(16) float rowj[2][32];      // row j of the panel
+  __align__(16) float dsum[2][32];      // per-column dot totals
+  __align__(16) float slot[2][64];      // cluster-visible partials: [column dots | pivot row]
+  float tau[32];           // reflector coefficients (CTA 0)
+  float G[32][33];         // G[c][j] = v_c . v_j, c < j (CTA 0)
   float T[32][33];         // T factor (CTA 0)
 };
+
+// LARFT T from G[c][j] = v_c . v_j (c < j) and tau, by one warp (lane = row of T):
+// T[i][j] = -tau_j sum_{i <= c < j} T[i][c] G[c][j], T[j][j] = tau_j (submission.py:129-137).
+__device__ __forceinline__ void larft_from_gram(float (&T)[32][33], const float (&G)[32][33], const float* tau,
+                                                int jmax) {
+  const int lane = threadIdx.x & 31;
+  for (int j = 0; j < jmax; ++j) {
+    float acc = 0.f;
+    for (int c = 0; c < j; ++c) {
+      const float t = T[lane][c];
+      acc = (c >= lane) ? fmaf(t, G[c][j], acc) : acc;
+    }
+    const float tj = tau[j];
+    T[lane][j] = (lane < j) ? -tj * acc : (lane == j ? tj : 0.f);
+    __syncwarp();
+  }
+}
 
 // Factor the panel whose column `warp` this warp holds in a[] (rows lane + 32 i of the
 // CTA's row block, p = cluster rank). All threads of the CTA -- and of the cluster when
@@ -100,29 +169,48 @@ __device__ __forceinline__ void factor_panel_cols(float (&a)[RPL], const int w, 
         sh.slot[ph][32 + c] = (p == 0) ? sh.rowj[ph][c] : 0.f;
       }
       cluster.sync();
-      // Gather the CTA partials in one round: lane q < cluster_size reads CTA q's slot for this
-      // warp's column and for the pivot column, lane 0 of CTA 0's slot also holds the pivot row.
-      float dd = 0.f, xx = 0.f, pv = 0.f;
-      if (lane < cluster_size) {
-        const float* rq = cluster.map_shared_rank(&sh.slot[ph][0], lane);
-        dd = rq[c];
-        xx = rq[j];
-      } else if (lane == 8 || lane == 9) {  // pivot-row entries a[j][j] and a[j][c] from CTA 0
-        pv = cluster.map_shared_rank(&sh.slot[ph][0], 0)[32 + (lane == 8 ? j : c)];
-      }
+      // One warp gathers the cluster in a single DSMEM round trip: lane l reads columns
+      // 16 (l % 2) .. +15 of CTA l / 2's partial dots (four 16-byte loads; clusters of up to 16
+      // CTAs), the sums over CTAs are formed with four xor shuffles, and lanes 0..1 also fetch
+      // the pivot row from CTA 0. Totals are published in this CTA's shared memory.
+      if (c == 0) {
+        const int q = lane >> 1, cg = lane & 1;
+        float4 v[4], pr[4];
 #pragma unroll
-      for (int o = 4; o >= 1; o >>= 1) {  // cluster_size <= 8
-        dd += __shfl_xor_sync(kFullMask, dd, o);
-        xx += __shfl_xor_sync(kFullMask, xx, o);
+        for (int t = 0; t < 4; ++t) v[t] = pr[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q < cluster_size) {
+          const float* rq = cluster.map_shared_rank(&sh.slot[ph][0], q) + 16 * cg;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) v[t] = *reinterpret_cast<const float4*>(rq + 4 * t);
+        }
+        if (q == 0) {
+          const float* r0 = cluster.map_shared_rank(&sh.slot[ph][0], 0) + 32 + 16 * cg;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) pr[t] = *reinterpret_cast<const float4*>(r0 + 4 * t);
+        }
+#pragma unroll
+        for (int o = 2; o <= 16; o <<= 1) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            v[t].x += __shfl_xor_sync(kFullMask, v[t].x, o);
+            v[t].y += __shfl_xor_sync(kFullMask, v[t].y, o);
+            v[t].z += __shfl_xor_sync(kFullMask, v[t].z, o);
+            v[t].w += __shfl_xor_sync(kFullMask, v[t].w, o);
+          }
+        }
+        if (q == 0) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            *reinterpret_cast<float4*>(&sh.dsum[ph][16 * cg + 4 * t]) = v[t];
+            *reinterpret_cast<float4*>(&sh.rowj[ph][16 * cg + 4 * t]) = pr[t];
+          }
+        }
       }
-      d = __shfl_sync(kFullMask, dd, 0);
-      xn2 = __shfl_sync(kFullMask, xx, 0);
-      alpha = __shfl_sync(kFullMask, pv, 8);
-      ajc = __shfl_sync(kFullMask, pv, 9);
-      if (HAS_T) {  // cluster totals for the T column built by warp j of CTA 0
-        if (lane == 0) sh.dsum[ph][c] = d;
-        __syncthreads();
-      }
+      __syncthreads();
+      d = sh.dsum[ph][c];
+      xn2 = sh.dsum[ph][j];
+      alpha = sh.rowj[ph][j];
+      ajc = sh.rowj[ph][c];
     }
     // (d) reflector and updates.
     const Reflector rf = make_reflector(alpha, xn2);
@@ -142,17 +230,17 @@ __device__ __forceinline__ void factor_panel_cols(float (&a)[RPL], const int w, 
         if (lr > j) a[i] *= rf.scale;
         else if (lr == j) a[i] = rf.diag;
       }
-      if (p == 0) {
-        if (lane == 0) tau_out[j] = rf.tau;
-        if (HAS_T) {
-          float acc = 0.f;
-          for (int cc = lane; cc < j; ++cc)
-            acc = fmaf(sh.T[lane][cc], fmaf(rf.scale, sh.dsum[ph][cc], sh.rowj[ph][cc]), acc);
-          if (lane < j) sh.T[lane][j] = -rf.tau * acc;
-          if (lane == j) sh.T[j][j] = rf.tau;
-        }
+      if (p == 0 && lane == 0) {
+        tau_out[j] = rf.tau;
+        sh.tau[j] = rf.tau;
       }
+    } else if (HAS_T && c < j && p == 0 && lane == 0) {
+      sh.G[c][j] = fmaf(rf.scale, d, ajc);  // v_c . v_j = a[j][c] + scale * (x_j . v_c)
     }
+  }
+  if (HAS_T && p == 0) {
+    __syncthreads();
+    if (c == 0) larft_from_gram(sh.T, sh.G, sh.tau, jmax);
   }
 }
 
@@ -243,19 +331,7 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
   }
   if (HAS_T) {
     __syncthreads();
-    if (g == 0) {
-      // LARFT: T[i][j] = -tau_j sum_{i<=c<j} T[i][c] G[c][j], T[j][j] = tau_j (lane i = row).
-      for (int j = 0; j < jmax; ++j) {
-        float acc = 0.f;
-        for (int c = 0; c < j; ++c) {
-          const float t = sh.T[lane][c];
-          acc = (c >= lane) ? fmaf(t, sh.G[c][j], acc) : acc;
-        }
-        const float tj = sh.tau[j];
-        sh.T[lane][j] = (lane < j) ? -tj * acc : (lane == j ? tj : 0.f);
-        __syncwarp();
-      }
-    }
+    if (g == 0) larft_from_gram(sh.T, sh.G, sh.tau, jmax);
   }
 }
 
@@ -269,34 +345,34 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_own
   const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
   const int n = P.n, k = P.k, w = P.w;
   const int m = n - k;
+  constexpr int R = 32 * RPL;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  float* stage = reinterpret_cast<float*>(smem_raw);  // 32 x (R + 1) floats
   const float* __restrict__ S = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   if (HAS_T)
     for (int i = threadIdx.x; i < 32 * 33; i += 32 * NW) (&sh.T[0][0])[i] = 0.f;
+  panel_stage_in(S, n, k, 0, R, min(R, m), w, stage, 32 * NW);
+  __syncthreads();
   float a[CPW][RPL];
 #pragma unroll
   for (int q = 0; q < CPW; ++q) {
     const int c = g + NW * q;
 #pragma unroll
-    for (int i = 0; i < RPL; ++i) {
-      const int lr = lane + 32 * i;
-      a[q][i] = (lr < m && c < w) ? S[(long long)(k + lr) * n + k + c] : 0.f;
-    }
+    for (int i = 0; i < RPL; ++i) a[q][i] = stage[c * (R + 1) + lane + 32 * i];
   }
   __syncthreads();
   factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
+  __syncthreads();
 #pragma unroll
   for (int q = 0; q < CPW; ++q) {
     const int c = g + NW * q;
-    if (c >= w) continue;
 #pragma unroll
-    for (int i = 0; i < RPL; ++i) {
-      const int lr = lane + 32 * i;
-      if (lr < m) Hb[(long long)(k + lr) * n + k + c] = a[q][i];
-    }
+    for (int i = 0; i < RPL; ++i) stage[c * (R + 1) + lane + 32 * i] = a[q][i];
   }
+  __syncthreads();
+  panel_stage_out(Hb, n, k, 0, R, min(R, m), w, stage, 32 * NW);
   if (HAS_T && P.T != nullptr) {
-    __syncthreads();
     float* Tb = P.T + (long long)bidx * P.t_bstride;
     for (int i = threadIdx.x; i < 32 * 32; i += 32 * NW) Tb[i] = sh.T[i / 32][i % 32];
   }
@@ -306,6 +382,8 @@ template <int RPL, bool HAS_T>
 __global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams P) {
   constexpr int R = 32 * RPL;
   __shared__ PanelShared<RPL> sh;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  float* stage = reinterpret_cast<float*>(smem_raw);  // 32 x (R + 1) floats
   cg::cluster_group cluster = cg::this_cluster();
   const int CP = (int)cluster.num_blocks();
   const int p = (int)cluster.block_rank();
@@ -313,36 +391,36 @@ __global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams
   const int lane = threadIdx.x & 31, c = threadIdx.x >> 5;
   const int n = P.n, k = P.k, w = P.w;
   const int m = n - k;
+  const int r0 = p * R;
+  const int rows_valid = max(0, min(R, m - r0));
   const float* __restrict__ S = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Hb = P.H + (long long)bidx * n * n;
 
   if (HAS_T)
     for (int i = threadIdx.x; i < 32 * 33; i += kPanelThreads) (&sh.T[0][0])[i] = 0.f;
-
+  panel_stage_in(S, n, k, r0, R, rows_valid, w, stage, kPanelThreads);
+  __syncthreads();
   float a[RPL];
 #pragma unroll
-  for (int i = 0; i < RPL; ++i) {
-    const int lr = p * R + lane + 32 * i;
-    a[i] = (lr < m && c < w) ? S[(long long)(k + lr) * n + k + c] : 0.f;
-  }
+  for (int i = 0; i < RPL; ++i) a[i] = stage[c * (R + 1) + lane + 32 * i];
   if (CP > 1) cluster.sync();  // every CTA of the cluster runs before any DSMEM access
   __syncthreads();
 
   factor_panel_cols<RPL, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k, CP, p);
 
-  if (c < w) {
+  __syncthreads();
 #pragma unroll
-    for (int i = 0; i < RPL; ++i) {
-      const int lr = p * R + lane + 32 * i;
-      if (lr < m) Hb[(long long)(k + lr) * n + k + c] = a[i];
-    }
-  }
+  for (int i = 0; i < RPL; ++i) stage[c * (R + 1) + lane + 32 * i] = a[i];
+  __syncthreads();
+  panel_stage_out(Hb, n, k, r0, R, rows_valid, w, stage, kPanelThreads);
   if (HAS_T && P.T != nullptr && p == 0) {
-    __syncthreads();
     float* Tb = P.T + (long long)bidx * P.t_bstride;
     for (int i = threadIdx.x; i < 32 * 32; i += kPanelThreads) Tb[i] = sh.T[i / 32][i % 32];
   }
   if (CP > 1) cluster.sync();  // keep this CTA's shared memory alive for remote readers
 }
+
+template <int RPL>
+constexpr size_t panel_stage_bytes() { return (size_t)32 * (32 * RPL + 1) * sizeof(float); }
 
 }  // namespace qrb200

@@ -25,8 +25,8 @@
 namespace qrb200 {
 
 constexpr int kNB = 32;              // panel width of the blocked path
-constexpr int kPanelRows = 512;      // panel rows per CTA of a cluster (32 lanes x 16 rows)
-constexpr int kMaxCluster = 8;       // portable cluster size
+constexpr int kPanelRows = 256;      // panel rows per CTA of a cluster (32 lanes x 8 rows)
+constexpr int kMaxCluster = 16;      // non-portable cluster size (one GPC)
 constexpr int kMaxN = kPanelRows * kMaxCluster;        // 4096
 constexpr int kSmallN = 128;         // whole-matrix single-CTA path up to this order
 
@@ -164,10 +164,19 @@ static int check_device() {
 
 template <int RPL, bool HAS_T>
 static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)panel_stage_bytes<RPL>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
   cfg.blockDim = dim3(kPanelThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = panel_stage_bytes<RPL>();
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -203,7 +212,14 @@ static cudaError_t run_small(const float* A, float* H, float* tau, long long bat
 
 template <int RPL, int CPW>
 static cudaError_t launch_owner(const PanelParams& pp, long long batch, cudaStream_t s) {
-  panel_owner_kernel<RPL, CPW, true><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), 0, s>>>(pp);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(panel_owner_kernel<RPL, CPW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)panel_stage_bytes<RPL>());
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  panel_owner_kernel<RPL, CPW, true><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), panel_stage_bytes<RPL>(), s>>>(pp);
   return cudaGetLastError();
 }
 
@@ -228,14 +244,16 @@ static cudaError_t launch_owner_cpw(const PanelParams& pp, long long batch, cuda
 
 // Panel kernel shape by panel height: panels up to 512 rows are factored by one CTA
 // ("owner computes" form, rows spread over the lanes of each column's warp); taller panels
-// use a cluster of ceil(m / 512) CTAs of 32 warps (one per column).
+// use a cluster of CTAs of 32 warps (one per column): two CTAs of 512 rows up to m = 1024,
+// then ceil(m / 256) CTAs of 256 rows (at most 16).
 static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s, long long t_bstride) {
   PanelParams q = pp;
   q.t_bstride = t_bstride;
   if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
   if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
   if (m <= 512) return launch_owner_cpw<16>(q, batch, s);
-  return launch_panel<16, true>(q, cdiv(m, kPanelRows), batch, s);
+  if (m <= 1024) return launch_panel<16, true>(q, cdiv(m, 512), batch, s);
+  return launch_panel<8, true>(q, cdiv(m, kPanelRows), batch, s);
 }
 
 // Trailing-update implementation for 32-wide panels: CUDA cores (default: at this width the

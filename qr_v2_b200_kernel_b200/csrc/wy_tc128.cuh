@@ -24,13 +24,17 @@ constexpr int kOB = 128;  // outer block width (reflectors per fat update)
 
 // ---------------------------------------------------------------------------------------
 // W^T = C^T V (or G = V^T V) over one row split; M = 128 trailing columns (or V columns),
-// N = W, K = rows in 32-row stages.
+// N = W, K = rows in 16-row stages. Both operands MN-major SW128_32B (K atoms of 4 rows,
+// SBO = (MN / 32) * 512). Two 32 KB stages (3 CTAs per SM); each thread prefetches the next
+// stage's global data into registers before the current stage's MMAs are issued, so HBM
+// latency overlaps tensor-core work.
+constexpr int kWChunk = 16;
 template <int W>
 struct VtcwStage {
-  float c_hi[kTcChunk * kTcCols];
-  float c_lo[kTcChunk * kTcCols];
-  float v_hi[kTcChunk * W];
-  float v_lo[kTcChunk * W];
+  float c_hi[kWChunk * kTcCols];
+  float c_lo[kWChunk * kTcCols];
+  float v_hi[kWChunk * W];
+  float v_lo[kWChunk * W];
 };
 template <int W>
 struct VtcwShared {
@@ -46,6 +50,8 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   VtcwShared<W>& sh = *reinterpret_cast<VtcwShared<W>*>(align1024(smem_raw));
   constexpr uint32_t LBO = 512, SBO_C = (kTcCols / 32) * 512, SBO_V = (W / 32) * 512;
+  constexpr int NV = W / 32;        // float4 of V per thread per stage (16 x W / 4 / 128)
+  constexpr int NC = GRAM ? 0 : 4;  // float4 of C per thread per stage (16 x 128 / 4 / 128)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bidx = blockIdx.z, split = blockIdx.y;
   const int n = P.n, k = P.k, w = P.w, m = n - k;
@@ -55,7 +61,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   const int r_begin = split * P.rows_per_split;
   const int r_end = min(m, r_begin + P.rows_per_split);
-  const int nchunks = r_end > r_begin ? (r_end - r_begin + kTcChunk - 1) / kTcChunk : 0;
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kWChunk - 1) / kWChunk : 0;
 
   if (tid == 0) {
     mbar_init(&sh.mbar[0], 1);
@@ -71,16 +77,25 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
   bool ok = true;
   const int q8 = lane & 7, kr = lane >> 3;
 
-  for (int ch = 0; ch < nchunks; ++ch) {
-    const int s = ch & 1;
-    VtcwStage<W>& st = sh.st[s];
-    if (ch >= 2) ok = mbar_wait(&sh.mbar[s], ((ch >> 1) - 1) & 1) && ok;
-    const int r0 = r_begin + ch * kTcChunk;
-    // V chunk: W/32 x 8 atoms of the unit lower trapezoid (columns >= w are zero).
+  // Element coordinates of this thread's float4 pieces: atom a covers 4 rows x 32 columns and
+  // is written by one warp (lane -> row a%4.., 16-byte piece).
+  auto v_coord = [&](int it, int& c, int& kk) {
+    const int atom = it * 4 + warp;
+    c = (atom % NV) * 32 + 4 * q8;
+    kk = (atom / NV) * 4 + kr;
+  };
+  auto c_coord = [&](int it, int& mn, int& kk) {
+    const int atom = it * 4 + warp;
+    mn = (atom & 3) * 32 + 4 * q8;
+    kk = (atom >> 2) * 4 + kr;
+  };
+  float4 pv[NV], pc[NC > 0 ? NC : 1];
+  auto load = [&](int ch) {
+    const int r0 = r_begin + ch * kWChunk;
 #pragma unroll
-    for (int it = 0; it < W / 16; ++it) {
-      const int atom = it * 4 + warp;
-      const int c = (atom % (W / 32)) * 32 + 4 * q8, kk = (atom / (W / 32)) * 4 + kr;
+    for (int it = 0; it < NV; ++it) {
+      int c, kk;
+      v_coord(it, c, kk);
       const int r = r0 + kk;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
       if (r < r_end && c < w) {
@@ -90,27 +105,43 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
         x.z = (c + 2 >= w) ? 0.f : ((r > c + 2) ? h.z : (r == c + 2 ? 1.f : 0.f));
         x.w = (c + 3 >= w) ? 0.f : ((r > c + 3) ? h.w : (r == c + 3 ? 1.f : 0.f));
       }
+      pv[it] = x;
+    }
+#pragma unroll
+    for (int it = 0; it < NC; ++it) {
+      int mn, kk;
+      c_coord(it, mn, kk);
+      const int r = r0 + kk, col = col0 + mn;
+      pc[it] = (r < r_end && col < nc) ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + col)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (nchunks > 0) load(0);
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int s = ch & 1;
+    VtcwStage<W>& st = sh.st[s];
+    if (ch >= 2) ok = mbar_wait(&sh.mbar[s], ((ch >> 1) - 1) & 1) && ok;
+#pragma unroll
+    for (int it = 0; it < NV; ++it) {
+      int c, kk;
+      v_coord(it, c, kk);
       float4 hi, lo;
-      split4(x, hi, lo);
+      split4(pv[it], hi, lo);
       const uint32_t off = sw32_off(c, kk, LBO, SBO_V) >> 2;
       *reinterpret_cast<float4*>(st.v_hi + off) = hi;
       *reinterpret_cast<float4*>(st.v_lo + off) = lo;
     }
-    if (!GRAM) {
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int atom = it * 4 + warp;
-        const int mn = (atom & 3) * 32 + 4 * q8, kk = (atom >> 2) * 4 + kr;
-        const int r = r0 + kk, col = col0 + mn;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < r_end && col < nc) x = *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + col);
-        float4 hi, lo;
-        split4(x, hi, lo);
-        const uint32_t off = sw32_off(mn, kk, LBO, SBO_C) >> 2;
-        *reinterpret_cast<float4*>(st.c_hi + off) = hi;
-        *reinterpret_cast<float4*>(st.c_lo + off) = lo;
-      }
+    for (int it = 0; it < NC; ++it) {
+      int mn, kk;
+      c_coord(it, mn, kk);
+      float4 hi, lo;
+      split4(pc[it], hi, lo);
+      const uint32_t off = sw32_off(mn, kk, LBO, SBO_C) >> 2;
+      *reinterpret_cast<float4*>(st.c_hi + off) = hi;
+      *reinterpret_cast<float4*>(st.c_lo + off) = lo;
     }
+    if (ch + 1 < nchunks) load(ch + 1);  // in flight while this stage's MMAs run
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -120,7 +151,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
       const uint32_t sbo_a = GRAM ? SBO_V : SBO_C;
       const uint32_t bvh = smem_u32(st.v_hi), bvl = smem_u32(st.v_lo);
 #pragma unroll
-      for (int ks = 0; ks < kTcChunk / 8; ++ks) {
+      for (int ks = 0; ks < kWChunk / 8; ++ks) {
         mma_tf32x3(tmem, make_sdesc_sw32(ach + ks * 2 * sbo_a, LBO, sbo_a), make_sdesc_sw32(acl + ks * 2 * sbo_a, LBO, sbo_a),
                    make_sdesc_sw32(bvh + ks * 2 * SBO_V, LBO, SBO_V), make_sdesc_sw32(bvl + ks * 2 * SBO_V, LBO, SBO_V),
                    idesc, ch > 0 || ks > 0);
@@ -236,16 +267,18 @@ struct Gemm128Params {
   int cend;               // MODE_UPD: trailing columns [k + w, cend)
 };
 
+// Stages hold a 16-wide K slice of both operands (K-major, no swizzle: CS = 128 B between
+// column quads, RS = 512 B between 8-row groups): 32 KB per stage, two stages, 3 CTAs per SM.
+constexpr int kGChunk = 16;
 struct Gemm128Stage {
-  float a_hi[128 * 32];
-  float a_lo[128 * 32];
-  float b_hi[128 * 32];
-  float b_lo[128 * 32];
+  float a_hi[128 * kGChunk];
+  float a_lo[128 * kGChunk];
+  float b_hi[128 * kGChunk];
+  float b_lo[128 * kGChunk];
 };
 struct Gemm128Shared {
   Gemm128Stage st[2];
   uint64_t mbar[2];
-  uint64_t done;
   uint32_t tmem;
 };
 constexpr size_t kGemm128Smem = sizeof(Gemm128Shared) + 1024;
@@ -254,7 +287,8 @@ template <int MODE>
 __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   Gemm128Shared& sh = *reinterpret_cast<Gemm128Shared*>(align1024(smem_raw));
-  constexpr uint32_t RS = 1024, CS = 128;  // 32-wide K chunk: 8 column quads per 8-row group
+  constexpr uint32_t RS = (kGChunk / 4) * 128, CS = 128;
+  constexpr int NK = kOB / kGChunk;  // K stages
   const int tid = threadIdx.x, warp = tid >> 5;
   const int bidx = blockIdx.z;
   const int n = P.n, k = P.k, w = P.w, m = n - k;
@@ -266,7 +300,6 @@ __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
   if (tid == 0) {
     mbar_init(&sh.mbar[0], 1);
     mbar_init(&sh.mbar[1], 1);
-    mbar_init(&sh.done, 1);
     fence_async_smem();
   }
   if (warp == 0) tmem_alloc(&sh.tmem, 128);
@@ -277,17 +310,22 @@ __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
   constexpr uint32_t idesc = make_idesc_tf32(128, 128, false, false);
   bool ok = true;
 
-  for (int kc = 0; kc < 4; ++kc) {
-    const int s = kc & 1;
-    Gemm128Stage& st = sh.st[s];
-    if (kc >= 2) ok = mbar_wait(&sh.mbar[s], 0) && ok;
-    // A tile: 128 rows x 32 K (columns 32 kc .. 32 kc + 31 of V or Y).
+  // Piece it of this thread: row rr of the tile, column quad cq of the K slice (8 lanes fill
+  // one 128-byte core matrix).
+  auto coord = [&](int it, int& rr, int& cq) {
+    const int idx = it * 128 + tid;
+    rr = (idx & 7) + 8 * (idx >> 5);
+    cq = (idx >> 3) & 3;
+  };
+  float4 pa[4], pb[4];
+  auto load = [&](int kc) {
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int idx = it * 128 + tid;
-      const int rr = (idx & 7) + 8 * (idx >> 6);
-      const int cq = (idx >> 3) & 7;
-      const int r = row0 + rr, c = 32 * kc + 4 * cq;
+    for (int it = 0; it < 4; ++it) {
+      int rr, cq;
+      coord(it, rr, cq);
+      const int c = kc * kGChunk + 4 * cq;
+      // A: rows of V (unit lower, MODE_Y) or of Y (MODE_UPD)
+      const int r = row0 + rr;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
       if (r < m && c < w) {
         if (MODE == MODE_Y) {
@@ -300,37 +338,44 @@ __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
           x = *reinterpret_cast<const float4*>(Yb + (long long)r * kOB + c);
         }
       }
-      float4 hi, lo;
-      split4(x, hi, lo);
-      const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
-      *reinterpret_cast<float4*>(st.a_hi + off) = hi;
-      *reinterpret_cast<float4*>(st.a_lo + off) = lo;
-    }
-    // B tile: 128 rows (N) x 32 K.
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int idx = it * 128 + tid;
-      const int rr = (idx & 7) + 8 * (idx >> 6);
-      const int cq = (idx >> 3) & 7;
-      const int j = col0 + rr, c = 32 * kc + 4 * cq;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      pa[it] = x;
+      // B: rows of T (MODE_Y) or trailing columns of sum_s W^T (MODE_UPD)
+      const int j = col0 + rr;
+      float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j < ncols && c < w) {
         if (MODE == MODE_Y) {
-          x = *reinterpret_cast<const float4*>(P.T + ((long long)bidx * kOB + j) * kOB + c);
+          y = *reinterpret_cast<const float4*>(P.T + ((long long)bidx * kOB + j) * kOB + c);
         } else {
           for (int q = 0; q < P.nsplit; ++q) {
             const float4 t = *reinterpret_cast<const float4*>(
                 P.Wp + (((long long)bidx * P.nsplit + q) * P.ncmax + j) * kOB + c);
-            x.x += t.x; x.y += t.y; x.z += t.z; x.w += t.w;
+            y.x += t.x; y.y += t.y; y.z += t.z; y.w += t.w;
           }
         }
       }
-      float4 hi, lo;
-      split4(x, hi, lo);
+      pb[it] = y;
+    }
+  };
+
+  load(0);
+  for (int kc = 0; kc < NK; ++kc) {
+    const int s = kc & 1;
+    Gemm128Stage& st = sh.st[s];
+    if (kc >= 2) ok = mbar_wait(&sh.mbar[s], ((kc >> 1) - 1) & 1) && ok;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      int rr, cq;
+      coord(it, rr, cq);
       const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
+      float4 hi, lo;
+      split4(pa[it], hi, lo);
+      *reinterpret_cast<float4*>(st.a_hi + off) = hi;
+      *reinterpret_cast<float4*>(st.a_lo + off) = lo;
+      split4(pb[it], hi, lo);
       *reinterpret_cast<float4*>(st.b_hi + off) = hi;
       *reinterpret_cast<float4*>(st.b_lo + off) = lo;
     }
+    if (kc + 1 < NK) load(kc + 1);  // in flight while this stage's MMAs run
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -338,41 +383,55 @@ __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
       const uint32_t ah = smem_u32(st.a_hi), al = smem_u32(st.a_lo);
       const uint32_t bh = smem_u32(st.b_hi), bl = smem_u32(st.b_lo);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
+      for (int ks = 0; ks < kGChunk / 8; ++ks)
         mma_tf32x3(tmem, make_sdesc(ah + ks * 2 * CS, CS, RS), make_sdesc(al + ks * 2 * CS, CS, RS),
                    make_sdesc(bh + ks * 2 * CS, CS, RS), make_sdesc(bl + ks * 2 * CS, CS, RS), idesc,
                    kc > 0 || ks > 0);
-      // Stages 0 and 1 are refilled once (chunks 2 and 3): their first MMA batches signal
-      // mbar[s]; the last batch signals `done`, whose single phase covers every MMA issued.
-      if (kc < 2) mma_commit(&sh.mbar[s]);
-      if (kc == 3) mma_commit(&sh.done);
+      mma_commit(&sh.mbar[s]);
     }
   }
-  ok = mbar_wait(&sh.done, 0) && ok;
-  tc_fence_after();
-  // Epilogue: thread t owns tile row t (TMEM lane t).
+  // Epilogue: thread t owns tile row t (TMEM lane t). The C slice for the next 32 columns is
+  // requested before the current one is processed.
   const int r = row0 + tid;
+  const bool row_ok = r < m;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
+  const long long roff = (long long)(k + r) * n + k + w;
+  float4 cv[8];
+  auto load_c = [&](int q) {
+    const int cbase = col0 + q * 32;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      cv[e] = (MODE == MODE_UPD && row_ok && cbase + 4 * e < ncols)
+                  ? *reinterpret_cast<const float4*>(Sb + roff + cbase + 4 * e)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  if (MODE == MODE_UPD) load_c(0);
+  {
+    const int last = NK - 1;
+    ok = mbar_wait(&sh.mbar[last & 1], (last >> 1) & 1) && ok;
+  }
+  tc_fence_after();
 #pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     float pv[32];
     tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, pv);
-    if (!ok || r >= m) continue;
+    float4 cur[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cur[e] = cv[e];
+    if (MODE == MODE_UPD && q + 1 < 4) load_c(q + 1);
+    if (!ok || !row_ok) continue;
     const int cbase = col0 + q * 32;
     if (MODE == MODE_Y) {
       float* yrow = P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + cbase;
 #pragma unroll
       for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(yrow + e) = make_float4(pv[e], pv[e + 1], pv[e + 2], pv[e + 3]);
     } else {
-      const long long off = (long long)(k + r) * n + k + w + cbase;
-      const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
-      float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        if (cbase + e < ncols) {
-          const float4 c = *reinterpret_cast<const float4*>(Sb + off + e);
-          *reinterpret_cast<float4*>(Ho + off + e) =
-              make_float4(c.x - pv[e], c.y - pv[e + 1], c.z - pv[e + 2], c.w - pv[e + 3]);
-        }
+      for (int e = 0; e < 8; ++e) {
+        if (cbase + 4 * e < ncols)
+          *reinterpret_cast<float4*>(Ho + roff + cbase + 4 * e) =
+              make_float4(cur[e].x - pv[4 * e], cur[e].y - pv[4 * e + 1], cur[e].z - pv[4 * e + 2], cur[e].w - pv[4 * e + 3]);
       }
     }
   }
