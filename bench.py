@@ -92,10 +92,9 @@ def allmax(dist, x: float) -> float:
 
 
 def shard(batch: int, world: int, rank: int):
-    per = -(-batch // world)
-    lo = min(batch, rank * per)
-    hi = min(batch, lo + per)
-    return lo, hi
+    from qr_v2_b200_kernel_b200.sharding import shard_range
+
+    return shard_range(batch, world, rank)
 
 
 # ----------------------------------------------------------------------------- clocks
