@@ -209,12 +209,25 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
   TbuildShared& sh = *reinterpret_cast<TbuildShared*>(smem_raw);
   const int b = blockIdx.x, tid = threadIdx.x;
   const int ow = P.ow;
-  for (int e = tid; e < kOB * kOB; e += 256) {
-    const int i = e / kOB, j = e % kOB;
-    float s = 0.f;
-    for (int q = 0; q < P.nsplit; ++q) s += P.Gp[(((long long)b * P.nsplit + q) * kOB + i) * kOB + j];
-    sh.G[i][j] = s;
-    sh.T[i][j] = 0.f;
+  // Sum the Gram partials: 16 float4 per thread, all loads of a split issued together.
+  {
+    float4 g[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) g[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < P.nsplit; ++q) {
+      const float4* src = reinterpret_cast<const float4*>(P.Gp + ((long long)b * P.nsplit + q) * kOB * kOB);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const float4 x = src[t * 256 + tid];
+        g[t].x += x.x; g[t].y += x.y; g[t].z += x.z; g[t].w += x.w;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int e = 4 * (t * 256 + tid), i = e / kOB, j = e % kOB;
+      sh.G[i][j] = g[t].x; sh.G[i][j + 1] = g[t].y; sh.G[i][j + 2] = g[t].z; sh.G[i][j + 3] = g[t].w;
+      sh.T[i][j] = 0.f; sh.T[i][j + 1] = 0.f; sh.T[i][j + 2] = 0.f; sh.T[i][j + 3] = 0.f;
+    }
   }
   __syncthreads();  // the zero fill must land before the diagonal blocks are written
   for (int e = tid; e < 4 * 32 * 32; e += 256) {
@@ -222,23 +235,45 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
     if (32 * blk < ow) sh.T[32 * blk + i][32 * blk + j] = P.Tin[(long long)b * 4096 + e];
   }
   __syncthreads();
+  // Register-tiled block steps: thread (ti, tj) owns rows ti + 8 q (q < r/8... up to 12) of
+  // column tj of the new 32-column block, so every shared load feeds several independent
+  // FMA chains.
+  const int tj = tid & 31, ti = tid >> 5;  // 32 columns x 8 row phases
   for (int bb = 1; bb * 32 < ow; ++bb) {
     const int r = 32 * bb;  // rows of the new column block
-    // X = G[0:r, r:r+32] T_bb
-    for (int e = tid; e < r * 32; e += 256) {
-      const int i = e / 32, j = e % 32;
-      float s = 0.f;
-#pragma unroll 8
-      for (int c = 0; c <= j; ++c) s = fmaf(sh.G[i][r + c], sh.T[r + c][r + j], s);
-      sh.X[i][j] = s;
+    const int nq = r / 8;   // rows per thread: 4, 8 or 12
+    // X = G[0:r, r:r+32] T_bb     (T_bb upper triangular: c <= tj)
+    {
+      float acc[12];
+#pragma unroll
+      for (int q = 0; q < 12; ++q) acc[q] = 0.f;
+      for (int c = 0; c <= tj; ++c) {
+        const float t = sh.T[r + c][r + tj];
+#pragma unroll
+        for (int q = 0; q < 12; ++q)
+          if (q < nq) acc[q] = fmaf(sh.G[ti + 8 * q][r + c], t, acc[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 12; ++q)
+        if (q < nq) sh.X[ti + 8 * q][tj] = acc[q];
     }
     __syncthreads();
-    // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r,0:r] upper triangular)
-    for (int e = tid; e < r * 32; e += 256) {
-      const int i = e / 32, j = e % 32;
-      float s = 0.f;
-      for (int c = i; c < r; ++c) s = fmaf(sh.T[i][c], sh.X[c][j], s);
-      sh.T[i][r + j] = -s;
+    // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r, 0:r] upper triangular: c >= row)
+    {
+      float acc[12];
+#pragma unroll
+      for (int q = 0; q < 12; ++q) acc[q] = 0.f;
+      for (int c = ti; c < r; ++c) {
+        const float x = sh.X[c][tj];
+#pragma unroll
+        for (int q = 0; q < 12; ++q) {
+          const int i = ti + 8 * q;
+          if (q < nq && c >= i) acc[q] = fmaf(sh.T[i][c], x, acc[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 12; ++q)
+        if (q < nq) sh.T[ti + 8 * q][r + tj] = -acc[q];
     }
     __syncthreads();
   }
