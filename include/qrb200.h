@@ -38,7 +38,9 @@ enum {
   QRB200_ERR_WORKSPACE = 2,  /* workspace too small or not 256-byte aligned          */
   QRB200_ERR_CUDA = 3,       /* a CUDA runtime call or kernel launch failed          */
   QRB200_ERR_DEVICE = 4,     /* current device is not an sm_100 (B200-class) GPU     */
-  QRB200_ERR_TIMEOUT = 5     /* a device-side bounded wait expired (see device_status) */
+  QRB200_ERR_TIMEOUT = 5,    /* a device-side bounded wait expired (see device_status) */
+  QRB200_ERR_SCRATCH_LIMIT = 6 /* qrb200_geqrf_f32_noalloc: problem needs more scratch than
+                                  QRB200_NOALLOC_SCRATCH_BYTES                           */
 };
 
 /* Bytes of scratch that qrb200_geqrf_f32 needs for (batch, n).
@@ -63,6 +65,34 @@ int qrb200_version(void);
  * Uses a synchronous symbol copy (it waits for prior work on the legacy default stream);
  * call it after the stream that ran the QR has completed. */
 int qrb200_device_status(int* status_out);
+
+/* ---- allocation-free entry (no counterpart in the reference) ------------------------- */
+
+/* Size of the library's static device scratch used by qrb200_geqrf_f32_noalloc: 32 MiB.
+ * It covers every call with qrb200_workspace_bytes(batch, n) <= this: up to 1 matrix of n = 4096,
+ * 4 of n = 2048, 13 of n = 1024, 38 of n = 512 or 70 of n = 256 per call; n <= 128 needs no
+ * scratch at any batch size. */
+#define QRB200_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Same result as qrb200_geqrf_f32 (bit for bit), but the scratch is a file-scope static
+ * __device__ array of the library instead of a caller workspace, so neither the caller nor the
+ * library allocates device memory. For callers that cannot or should not allocate: plain C or
+ * FFI code with no device allocator at hand, loops that must not call cudaMalloc/cudaFree
+ * (cudaFree waits for the whole device), and processes whose device memory is already fully
+ * reserved by another allocator.
+ *   - Limit: returns QRB200_ERR_SCRATCH_LIMIT, launching nothing, when
+ *     qrb200_workspace_bytes(batch, n) > QRB200_NOALLOC_SCRATCH_BYTES; use qrb200_geqrf_f32
+ *     with a workspace for larger problems. Other errors are those of qrb200_geqrf_f32.
+ *   - Set-up: the first call on each device (the current device) looks up the array's device
+ *     address with cudaGetSymbolAddress, which loads the library module that holds it there;
+ *     make that first call before any stream capture on that device.
+ *   - Nothing needs to start at zero: every scratch word is written before it is read within
+ *     a call, so the array's contents between calls do not matter.
+ *   - One array per device: calls on the same device whose executions overlap (different
+ *     streams, or host threads, without ordering) race on it and give wrong results. Order
+ *     them on one stream, or with events. */
+int qrb200_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                             int64_t a_batch_stride, void* stream);
 
 /* ---- diagnostics (no counterpart in the reference; used by bench.py) ---------------- */
 

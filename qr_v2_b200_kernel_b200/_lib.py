@@ -18,6 +18,8 @@ QRB200_ERR_WORKSPACE = 2
 QRB200_ERR_CUDA = 3
 QRB200_ERR_DEVICE = 4
 QRB200_ERR_TIMEOUT = 5
+QRB200_ERR_SCRATCH_LIMIT = 6
+NOALLOC_SCRATCH_BYTES = 32 << 20  # QRB200_NOALLOC_SCRATCH_BYTES
 
 class KernelStat(ctypes.Structure):
     """``qrb200_kernel_stat`` of include/qrb200.h."""
@@ -32,6 +34,9 @@ SIGNATURES = {
     "qrb200_geqrf_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                         ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "qrb200_geqrf_f32_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                ctypes.c_void_p]),
     "qrb200_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "qrb200_version": (ctypes.c_int, []),
     "qrb200_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),

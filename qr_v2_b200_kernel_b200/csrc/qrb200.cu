@@ -518,6 +518,7 @@ using namespace qrb200;
 
 static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64_t n,
                       int64_t a_batch_stride, void* workspace, size_t workspace_bytes, void* stream);
+int qrb200_noalloc_scratch(void** out);  // noalloc.cu: static scratch of the current device
 
 extern "C" {
 
@@ -529,6 +530,21 @@ size_t qrb200_workspace_bytes(int64_t batch, int64_t n) {
 int qrb200_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
                      int64_t a_batch_stride, void* workspace, size_t workspace_bytes, void* stream) {
   return geqrf_impl(A, H, tau, batch, n, a_batch_stride, workspace, workspace_bytes, stream);
+}
+
+int qrb200_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch, int64_t n,
+                             int64_t a_batch_stride, void* stream) {
+  // Unsupported shapes get geqrf_impl's QRB200_ERR_ARG, not the scratch limit.
+  const bool shape_ok = batch >= 0 && n >= 0 && n <= kMaxN && batch <= 65535;
+  const size_t need = shape_ok ? qrb200_workspace_bytes(batch, n) : 0;
+  if (need > (size_t)QRB200_NOALLOC_SCRATCH_BYTES) return QRB200_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int st = qrb200_noalloc_scratch(&scratch);
+    if (st != QRB200_OK) return st;
+  }
+  return geqrf_impl(A, H, tau, batch, n, a_batch_stride, scratch, need ? (size_t)QRB200_NOALLOC_SCRATCH_BYTES : 0,
+                    stream);
 }
 
 long long qrb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
@@ -603,6 +619,9 @@ const char* qrb200_status_string(int status) {
     case QRB200_ERR_CUDA: return "CUDA runtime error or kernel launch failure";
     case QRB200_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
     case QRB200_ERR_TIMEOUT: return "device-side bounded wait expired";
+    case QRB200_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the 32 MiB static scratch of qrb200_geqrf_f32_noalloc; "
+             "call qrb200_geqrf_f32 with a workspace";
     default: return "unknown status";
   }
 }

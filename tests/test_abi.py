@@ -36,7 +36,7 @@ def test_library_exports_every_header_symbol(lib):
 
 def test_status_strings_and_version(lib):
     assert lib.qrb200_version() >= 100
-    for st in range(6):
+    for st in range(7):
         assert lib.qrb200_status_string(st)
     assert lib.qrb200_status_string(0) == b"ok"
 
@@ -78,3 +78,16 @@ def test_operator_rejects_bad_inputs_on_cpu():
         custom_kernel(torch.zeros(2, 4, 5))
     with pytest.raises(TypeError):
         custom_kernel([[1.0]])
+
+
+def test_noalloc_entry_host_checks(lib):
+    p = ctypes.c_void_p(16)
+    f = lib.qrb200_geqrf_f32_noalloc
+    assert f(p, p, p, -1, 8, 64, None) == _lib.QRB200_ERR_ARG
+    assert f(None, p, p, 1, 8, 64, None) == _lib.QRB200_ERR_ARG
+    assert f(p, p, p, 1, 1 << 20, 1 << 40, None) == _lib.QRB200_ERR_ARG
+    assert f(p, p, p, 70000, 512, 512 * 512, None) == _lib.QRB200_ERR_ARG  # batch limit, not scratch
+    assert f(p, p, p, 0, 512, 512 * 512, None) == _lib.QRB200_OK
+    # beyond the static scratch: rejected before any device call
+    assert lib.qrb200_workspace_bytes(2, 4096) > _lib.NOALLOC_SCRATCH_BYTES >= lib.qrb200_workspace_bytes(1, 4096)
+    assert f(p, p, p, 2, 4096, 4096 * 4096, None) == _lib.QRB200_ERR_SCRATCH_LIMIT
