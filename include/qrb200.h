@@ -70,7 +70,7 @@ int qrb200_device_status(int* status_out);
 
 /* Size of the library's static device scratch used by qrb200_geqrf_f32_noalloc: 32 MiB.
  * It covers every call with qrb200_workspace_bytes(batch, n) <= this: up to 1 matrix of n = 4096,
- * 4 of n = 2048, 13 of n = 1024, 38 of n = 512 or 70 of n = 256 per call; n <= 128 needs no
+ * 3 of n = 2048, 11 of n = 1024, 29 of n = 512 or 55 of n = 256 per call; n <= 128 needs no
  * scratch at any batch size. */
 #define QRB200_NOALLOC_SCRATCH_BYTES (32u << 20)
 

@@ -13,6 +13,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "../../include/qrb200.h"
@@ -111,7 +112,8 @@ struct Workspace {
   float* W2;    // batch x 32 x ncmax
   float* Tob;   // two-level: batch x 128 x 128 outer-block factors
   float* Gp;    // two-level: batch x nsplit_g x 128 x 128 Gram partials
-  float* Y;     // two-level: batch x n x 128  (V T^T)
+  float* Y;     // two-level: batch x n x 128  (V T^T), even outer blocks
+  float* Y2;    // two-level: same, odd outer blocks (look-ahead keeps two blocks' Y alive)
   float* Wf;    // two-level: batch x nsplit_f x n x 128 (W^T partials of the wide update)
   size_t bytes;
 };
@@ -147,31 +149,53 @@ static Workspace layout(long long batch, int n, void* base) {
   ws.Tob = carve((size_t)batch * kOB * kOB * f);
   ws.Gp = carve((size_t)batch * nsw * kOB * kOB * f);
   ws.Y = carve((size_t)batch * n * kOB * f);
+  ws.Y2 = carve((size_t)batch * n * kOB * f);
   ws.Wf = carve((size_t)batch * nsw * (size_t)n * kOB * f);
   return ws;
 }
 
+// Function attributes (shared-memory opt-in, cluster size) belong to each device's instance of
+// a kernel, so one-time set-up is tracked per device ordinal (devices >= 64 redo it every call).
+struct PerDevice {
+  std::atomic<unsigned long long> bits{0};
+  bool done(int dev) const { return dev < 64 && ((bits.load(std::memory_order_acquire) >> dev) & 1ull); }
+  void mark(int dev) {
+    if (dev < 64) bits.fetch_or(1ull << dev, std::memory_order_acq_rel);
+  }
+};
+
+static int current_device() {
+  int d = 0;
+  return cudaGetDevice(&d) == cudaSuccess ? d : 0;
+}
+
 static int check_device() {
-  static int cached = -1;
-  if (cached >= 0) return cached;
+  static PerDevice ok, bad;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return QRB200_ERR_CUDA;
+  if (ok.done(dev)) return QRB200_OK;
+  if (bad.done(dev)) return QRB200_ERR_DEVICE;
   int major = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return QRB200_ERR_CUDA;
-  cached = (major == 10) ? QRB200_OK : QRB200_ERR_DEVICE;
-  return cached;
+  if (major == 10) {
+    ok.mark(dev);
+    return QRB200_OK;
+  }
+  bad.mark(dev);
+  return QRB200_ERR_DEVICE;
 }
 
 template <int RPL, bool HAS_T>
 static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)panel_stage_bytes<RPL>());
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.mark(dev);
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
@@ -192,11 +216,12 @@ template <int NMAX>
 static cudaError_t launch_small(const float* A, float* H, float* tau, long long batch, int n,
                                 long long abs, cudaStream_t s) {
   const size_t smem = sizeof(SmallShared<NMAX>);
-  static bool configured = false;  // per instantiation; attribute is per device function
-  if (!configured) {
+  static PerDevice configured;  // per instantiation and device
+  const int dev = current_device();
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(small_qr_kernel<NMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.mark(dev);
   }
   small_qr_kernel<NMAX><<<(unsigned)batch, kPanelThreads, smem, s>>>(A, abs, H, tau, n);
   return cudaGetLastError();
@@ -212,12 +237,13 @@ static cudaError_t run_small(const float* A, float* H, float* tau, long long bat
 
 template <int RPL, int CPW>
 static cudaError_t launch_owner(const PanelParams& pp, long long batch, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
     cudaError_t e = cudaFuncSetAttribute(panel_owner_kernel<RPL, CPW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)panel_stage_bytes<RPL>());
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured.mark(dev);
   }
   panel_owner_kernel<RPL, CPW, true><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), panel_stage_bytes<RPL>(), s>>>(pp);
   return cudaGetLastError();
@@ -269,13 +295,14 @@ static bool use_tc_update(int n, const float* A, long long abs) {
 }
 
 static cudaError_t tc_configure() {
-  static bool done = false;
-  if (done) return cudaSuccess;
+  static PerDevice done;
+  const int dev = current_device();
+  if (done.done(dev)) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(tc_vtc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtcSmem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(tc_upd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpdSmem);
   if (e != cudaSuccess) return e;
-  done = true;
+  done.mark(dev);
   return cudaSuccess;
 }
 
@@ -366,15 +393,16 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
 
 
 static cudaError_t tc128_configure() {
-  static bool done = false;
-  if (done) return cudaSuccess;
+  static PerDevice done;
+  const int dev = current_device();
+  if (done.done(dev)) return cudaSuccess;
   cudaError_t e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_Y>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_UPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
-  done = true;
+  done.mark(dev);
   return cudaSuccess;
 }
 
@@ -413,13 +441,105 @@ static cudaError_t launch_narrow(const float* src, long long sbs, float* H, cons
   return cudaGetLastError();
 }
 
+// Look-ahead streams of one device: the critical chain (panels, narrow updates, T, Y and the
+// update of the next outer block's columns) runs on a high-priority stream, the rest of each
+// wide update on a low-priority one, forked from and joined back into the caller's stream.
+struct LookaheadStreams {
+  cudaStream_t p = nullptr, u = nullptr;
+  cudaEvent_t fork = nullptr, y = nullptr, u2 = nullptr, pj = nullptr, uj = nullptr;
+};
+constexpr int kMaxDevices = 64;
+static std::mutex g_la_mu[kMaxDevices];  // one two-level enqueue per device at a time
+static LookaheadStreams g_la[kMaxDevices];
+
+static cudaError_t lookahead_streams(int dev, LookaheadStreams** out) {
+  LookaheadStreams& L = g_la[dev];
+  if (!L.p) {
+    int least = 0, greatest = 0;
+    cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&L.u, cudaStreamNonBlocking, least);
+    for (cudaEvent_t* ev : {&L.fork, &L.y, &L.u2, &L.pj, &L.uj})
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&L.p, cudaStreamNonBlocking, greatest);
+    if (e != cudaSuccess) {
+      L.p = nullptr;  // retried on the next call
+      return e;
+    }
+  }
+  *out = &L;
+  return cudaSuccess;
+}
+
+// QRB200_LOOKAHEAD=0 keeps the whole two-level schedule on the caller's stream.
+static bool lookahead_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_LOOKAHEAD");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// 128-wide update of trailing columns [coff, cend - k0 - ow) (relative to k0 + ow) by the
+// outer block at k0: W^T = C^T V per row split, then C -= Y W. coff is a multiple of 128, so
+// every column sees the same tiles, and the same arithmetic, however the range is cut.
+static cudaError_t launch_wide(const float* src, long long sbs, float* H, const float* Y, const Workspace& ws,
+                               long long batch, int n, int k0, int ow, int coff, int cend, cudaStream_t s) {
+  const int m = n - k0, nc = cend - k0 - ow - coff;
+  if (nc <= 0) return cudaSuccess;
+  const int nsw = cdiv(m, kRowsPerSplitWide);
+  const double bm = (double)batch * m;
+  WyParams wp{};
+  wp.src = src;
+  wp.src_bstride = sbs;
+  wp.H = H;
+  wp.Wp = ws.Wf;
+  wp.n = n;
+  wp.k = k0;
+  wp.w = ow;
+  wp.cend = cend;
+  wp.nsplit = nsw;
+  wp.rows_per_split = kRowsPerSplitWide;
+  wp.ncmax = n;
+  wp.coff = coff;
+  Gemm128Params gp{};
+  gp.H = H;
+  gp.src = src;
+  gp.src_bstride = sbs;
+  gp.Hout = H;
+  gp.T = ws.Tob;
+  gp.Y = const_cast<float*>(Y);
+  gp.y_bstride = (long long)n * kOB;
+  gp.Wp = ws.Wf;
+  gp.nsplit = nsw;
+  gp.ncmax = n;
+  gp.n = n;
+  gp.k = k0;
+  gp.w = ow;
+  gp.cend = cend;
+  gp.coff = coff;
+  {
+    LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
+    tc_vtcw_kernel<kOB, false><<<dim3(cdiv(nc, kTcCols), nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(wp);
+  }
+  {
+    LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
+    tc_gemm128_kernel<MODE_UPD><<<dim3(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
+  }
+  return cudaGetLastError();
+}
+
 // Two-level blocked QR: outer blocks of 128 columns, each factored as four 32-column panels
 // with narrow updates inside the block, then one 128-wide tensor-core update of the trailing
 // matrix, C <- C - Y (V^T C) with Y = V T^T (T assembled from the block Gram matrix).
-static cudaError_t run_two_level(const float* A, float* H, float* tau, long long batch, int n, long long abs,
-                                 const Workspace& ws, cudaStream_t s) {
-  cudaError_t e = tc128_configure();
-  if (e != cudaSuccess) return e;
+// With look-ahead (L != nullptr) the wide update is cut in two: the next outer block's 128
+// columns (U1, on the critical stream sp) and everything right of them (U2, on su), so U2 of
+// block k0 runs while block k0 + 128 is factored. U1 of block k0 + 128 waits for U2 of block
+// k0 (same columns); Y alternates between two buffers so U2 can still read block k0's.
+static cudaError_t two_level_body(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                  const Workspace& ws, cudaStream_t sp, cudaStream_t su, LookaheadStreams* L) {
+  cudaError_t e;
+  bool u2_pending = false;
   for (int k0 = 0; k0 < n; k0 += kOB) {
     const int ow = std::min(kOB, n - k0);
     for (int kb = k0; kb < k0 + ow; kb += kNB) {
@@ -431,20 +551,21 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
       PanelParams pp{src, sbs, H, tau, Tslot, n, kb, w};
       {
         LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
-        e = launch_panel_for(pp, m, batch, s, 4 * kNB * kNB);
+        e = launch_panel_for(pp, m, batch, sp, 4 * kNB * kNB);
       }
       if (e != cudaSuccess) return e;
       if (kb + w < k0 + ow) {
-        e = launch_narrow(src, sbs, H, Tslot, ws, batch, n, kb, w, k0 + ow, s);
+        e = launch_narrow(src, sbs, H, Tslot, ws, batch, n, kb, w, k0 + ow, sp);
         if (e != cudaSuccess) return e;
       }
     }
     if (k0 + ow >= n) break;
-    const int m = n - k0, nc = n - k0 - ow;
+    const int m = n - k0;
     const float* src = (k0 == 0) ? A : H;
     const long long sbs = (k0 == 0) ? abs : (long long)n * n;
     const int nsw = cdiv(m, kRowsPerSplitWide);
     const double bm = (double)batch * m;
+    float* Y = ((k0 / kOB) & 1) ? ws.Y2 : ws.Y;
     // Gram matrix of the outer block's reflectors.
     WyParams g{};
     g.src = H;
@@ -460,56 +581,67 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
     g.ncmax = kOB;
     {
       LaunchScope ls(K_GRAM, 2.0 * bm * ow * ow, 4.0 * bm * ow);
-      tc_vtcw_kernel<kOB, true><<<dim3(1, nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(g);
+      tc_vtcw_kernel<kOB, true><<<dim3(1, nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), sp>>>(g);
     }
     {
       TbuildParams tp{ws.Gp, nsw, ws.T, ws.Tob, ow};
       LaunchScope ls(K_TBUILD, batch * 2.0 * ow * ow * ow / 3.0, 4.0 * batch * (nsw + 1.0) * ow * ow);
-      tbuild_kernel<<<(unsigned)batch, 256, kTbuildSmem, s>>>(tp);
+      tbuild_kernel<<<(unsigned)batch, 256, kTbuildSmem, sp>>>(tp);
     }
     Gemm128Params gp{};
     gp.H = H;
-    gp.src = src;
-    gp.src_bstride = sbs;
-    gp.Hout = H;
     gp.T = ws.Tob;
-    gp.Y = ws.Y;
+    gp.Y = Y;
     gp.y_bstride = (long long)n * kOB;
-    gp.Wp = ws.Wf;
-    gp.nsplit = nsw;
-    gp.ncmax = n;
     gp.n = n;
     gp.k = k0;
     gp.w = ow;
-    gp.cend = n;
     {
       LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
-      tc_gemm128_kernel<MODE_Y><<<dim3(1, cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
+      tc_gemm128_kernel<MODE_Y><<<dim3(1, cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, sp>>>(gp);
     }
-    WyParams wp{};
-    wp.src = src;
-    wp.src_bstride = sbs;
-    wp.H = H;
-    wp.Wp = ws.Wf;
-    wp.n = n;
-    wp.k = k0;
-    wp.w = ow;
-    wp.cend = n;
-    wp.nsplit = nsw;
-    wp.rows_per_split = kRowsPerSplitWide;
-    wp.ncmax = n;
-    {
-      LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
-      tc_vtcw_kernel<kOB, false><<<dim3(cdiv(nc, kTcCols), nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(wp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int split_at = k0 + 2 * kOB;  // U1 = columns [k0 + ow, split_at), U2 = [split_at, n)
+    if (L == nullptr || split_at >= n) {
+      if (L != nullptr && u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;
+      u2_pending = false;
+      e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, 0, n, sp);
+      if (e != cudaSuccess) return e;
+      continue;
     }
-    {
-      LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
-      tc_gemm128_kernel<MODE_UPD><<<dim3(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
-    }
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if ((e = cudaEventRecord(L->y, sp)) != cudaSuccess) return e;
+    if (u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;  // U2 of k0 - 128
+    if ((e = cudaStreamWaitEvent(su, L->y, 0)) != cudaSuccess) return e;
+    if ((e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, kOB, n, su)) != cudaSuccess) return e;
+    if ((e = cudaEventRecord(L->u2, su)) != cudaSuccess) return e;
+    u2_pending = true;
+    if ((e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, 0, split_at, sp)) != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+static cudaError_t run_two_level(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                 const Workspace& ws, cudaStream_t s) {
+  cudaError_t e = tc128_configure();
+  if (e != cudaSuccess) return e;
+  const int dev = current_device();
+  // Serial schedule when profiling (per-launch events on one stream), when switched off, or
+  // when no outer block has columns beyond the next one (n <= 256).
+  if (t_prof || !lookahead_enabled() || n <= 2 * kOB || dev >= kMaxDevices)
+    return two_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
+  std::lock_guard<std::mutex> lk(g_la_mu[dev]);
+  LookaheadStreams* L = nullptr;
+  if ((e = lookahead_streams(dev, &L)) != cudaSuccess) return e;
+  if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
+  const cudaError_t body = two_level_body(A, H, tau, batch, n, abs, ws, L->p, L->u, L);
+  // Join both streams back into the caller's stream, also after a failed launch.
+  e = cudaEventRecord(L->pj, L->p);
+  if (e == cudaSuccess) e = cudaEventRecord(L->uj, L->u);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->pj, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->uj, 0);
+  return body != cudaSuccess ? body : e;
 }
 
 }  // namespace qrb200

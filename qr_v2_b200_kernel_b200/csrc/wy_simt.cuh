@@ -28,6 +28,7 @@ struct WyParams {
   int nsplit;             // row splits of the V^T C product
   int rows_per_split;     // multiple of 32
   int ncmax;              // leading dimension of Wp / W2 (>= cend - k - w)
+  int coff;               // 128-wide kernels: first trailing column (relative to k + w) of this launch
 };
 
 // V[r][c] of the panel starting at (k, k): unit lower trapezoid stored in H.

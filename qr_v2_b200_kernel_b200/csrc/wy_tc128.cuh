@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
   const int bidx = blockIdx.z, split = blockIdx.y;
   const int n = P.n, k = P.k, w = P.w, m = n - k;
   const int nc = GRAM ? w : P.cend - k - w;
-  const int col0 = blockIdx.x * kTcCols;
+  const int col0 = (GRAM ? 0 : P.coff) + blockIdx.x * kTcCols;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   const int r_begin = split * P.rows_per_split;
@@ -300,6 +300,7 @@ struct Gemm128Params {
   int nsplit, ncmax;
   int n, k, w;            // outer block: rows/columns from k, width w (<= 128)
   int cend;               // MODE_UPD: trailing columns [k + w, cend)
+  int coff;               // MODE_UPD: first trailing column of this launch (tile-aligned)
 };
 
 // Stages hold a 16-wide K slice of both operands (K-major, no swizzle: CS = 128 B between
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_kernel(Gemm128Params P) {
   const int bidx = blockIdx.z;
   const int n = P.n, k = P.k, w = P.w, m = n - k;
   const int ncols = (MODE == MODE_Y) ? kOB : P.cend - k - w;  // B rows (N extent)
-  const int col0 = blockIdx.x * 128, row0 = blockIdx.y * 128;
+  const int col0 = (MODE == MODE_UPD ? P.coff : 0) + blockIdx.x * 128, row0 = blockIdx.y * 128;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
 

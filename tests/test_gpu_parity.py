@@ -134,10 +134,72 @@ def test_deterministic_and_batch_independent():
 def test_runs_on_current_stream():
     A = gen.config_input("C3", device="cuda", batch=4)
     s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         H, tau = custom_kernel(A)
     s.synchronize()
     _assert_gate(A, H, tau, "side stream")
+
+
+def _profiled(A):
+    """The same factorisation through qrb200_profile_geqrf_f32 (every launch on the caller's
+    stream, one after another: no look-ahead)."""
+    import ctypes
+
+    from qr_v2_b200_kernel_b200 import _lib
+
+    lib = _lib.load()
+    b, n, _ = A.shape
+    H = torch.empty_like(A)
+    tau = torch.empty((b, n), device=A.device)
+    need = lib.qrb200_workspace_bytes(b, n)
+    ws = torch.empty(max(need, 256), dtype=torch.uint8, device=A.device)
+    stats = (_lib.KernelStat * 16)()
+    cnt = ctypes.c_int(0)
+    st = lib.qrb200_profile_geqrf_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), b, n, n * n, ws.data_ptr(), need,
+                                      torch.cuda.current_stream().cuda_stream, stats, 16, ctypes.byref(cnt))
+    assert st == 0
+    return H, tau
+
+
+@pytest.mark.parametrize("batch,n", [(3, 384), (4, 512), (2, 1000), (2, 1024)])
+def test_lookahead_schedule_matches_serial_schedule(batch, n):
+    # The look-ahead cuts each wide update at a 128-column tile boundary and runs part of it
+    # on a second stream; every column still sees the same tiles, so results agree bit for bit.
+    A = torch.randn(batch, n, n, device="cuda")
+    H, tau = _run(A)
+    Hs, taus = _profiled(A)
+    torch.cuda.synchronize()
+    assert torch.equal(H, Hs) and torch.equal(tau, taus)
+
+
+def test_concurrent_calls_from_host_threads():
+    import threading
+
+    As = [torch.randn(3, 512, 512, device="cuda") for _ in range(4)]
+    ref = [_run(A) for A in As]
+    out = [None] * len(As)
+    errors = []
+
+    def worker(i):
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.default_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    out[i] = custom_kernel(As[i])
+            s.synchronize()
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    ts = [threading.Thread(target=worker, args=(i,)) for i in range(len(As))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errors, errors
+    for (H, tau), (Hr, taur) in zip(out, ref):
+        assert torch.equal(H, Hr) and torch.equal(tau, taur)
 
 
 def test_error_paths_on_gpu():

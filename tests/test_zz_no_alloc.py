@@ -50,12 +50,23 @@ def _noalloc(lib, A):
     return H, tau
 
 
-# n <= 128 (no scratch), single-level (n % 4 != 0), two-level, and the largest shapes that fit.
-SHAPES = [(5, 96), (3, 200), (4, 256), (2, 512), (1, 1000), (38, 512), (13, 1024), (1, 4096)]
+def _max_batch(lib, n):
+    b = 0
+    while lib.qrb200_workspace_bytes(b + 1, n) <= _lib.NOALLOC_SCRATCH_BYTES:
+        b += 1
+    return b
+
+
+# n <= 128 (no scratch), single-level (n % 4 != 0), two-level, and the largest batches that fit
+# (batch None = the largest).
+SHAPES = [(5, 96), (3, 200), (4, 256), (2, 512), (1, 1000), (None, 512), (None, 1024), (1, 4096)]
 
 
 @pytest.mark.parametrize("batch,n", SHAPES)
 def test_noalloc_matches_workspace_entry_two_calls(lib, batch, n):
+    if batch is None:
+        batch = _max_batch(lib, n)
+        assert batch >= 8
     assert lib.qrb200_workspace_bytes(batch, n) <= _lib.NOALLOC_SCRATCH_BYTES
     g = torch.Generator(device="cuda").manual_seed(1000 * n + batch)
     for call in range(2):
@@ -84,7 +95,7 @@ def test_noalloc_launches_the_same_kernels(lib):
 
 
 def test_noalloc_rejects_problems_beyond_the_static_scratch(lib):
-    for b, n in [(2, 4096), (39, 512), (14, 1024)]:
+    for b, n in [(2, 4096), (_max_batch(lib, 512) + 1, 512), (_max_batch(lib, 1024) + 1, 1024)]:
         assert lib.qrb200_workspace_bytes(b, n) > _lib.NOALLOC_SCRATCH_BYTES
         A = torch.randn((b, n, n), device="cuda")
         H = torch.zeros_like(A)
