@@ -8,6 +8,15 @@ namespace qrb200 {
 
 constexpr unsigned kFullMask = 0xffffffffu;
 
+// Named CTA barriers (id 0 is __syncthreads): bar.sync waits for nthreads arrivals, bar.arrive
+// adds this warp's arrival without waiting.
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Transposed butterfly reduction of NV per-lane partial sums across a warp.
 // On return d[0 .. NV/32) of lane L hold the warp-wide sums of the original entries
 // L*(NV/32) + q. Each of the five xor steps halves the live array: the lane keeps the

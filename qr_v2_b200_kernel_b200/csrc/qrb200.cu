@@ -18,7 +18,9 @@
 
 #include "../../include/qrb200.h"
 #include "panel.cuh"
+#include "panel_la.cuh"
 #include "small.cuh"
+#include "small_fw.cuh"
 #include "wy_simt.cuh"
 #include "wy_tc.cuh"
 #include "wy_tc128.cuh"
@@ -227,10 +229,40 @@ static cudaError_t launch_small(const float* A, float* H, float* tau, long long 
   return cudaGetLastError();
 }
 
+template <int NMAX, int NWL>
+static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                   cudaStream_t s) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
+    cudaError_t e = cudaFuncSetAttribute(small_fw_kernel<NMAX, NWL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)small_fw_smem<NMAX>());
+    if (e != cudaSuccess) return e;
+    configured.mark(dev);
+  }
+  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n);
+  return cudaGetLastError();
+}
+
+// QRB200_SMALL=smem selects the earlier shared-memory whole-matrix kernel.
+static bool small_pipeline() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_SMALL");
+    v = (e && strcmp(e, "smem") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch.
 static cudaError_t run_small(const float* A, float* H, float* tau, long long batch, int n,
                              long long abs, cudaStream_t s) {
   LaunchScope ls(K_SMALL, batch * 4.0 * n * (double)n * n / 3.0, batch * 8.0 * n * (double)n);
+  if (small_pipeline()) {
+    if (n <= 32) return launch_small_fw<32, 8>(A, H, tau, batch, n, abs, s);
+    if (n <= 64) return launch_small_fw<64, 16>(A, H, tau, batch, n, abs, s);
+    return launch_small_fw<128, 16>(A, H, tau, batch, n, abs, s);
+  }
   if (n <= 64) return launch_small<64>(A, H, tau, batch, n, abs, s);
   return launch_small<128>(A, H, tau, batch, n, abs, s);
 }
@@ -268,16 +300,42 @@ static cudaError_t launch_owner_cpw(const PanelParams& pp, long long batch, cuda
   }
 }
 
+template <int RPL, int CPW>
+static cudaError_t launch_la(const PanelParams& pp, long long batch, cudaStream_t s) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
+    cudaError_t e = cudaFuncSetAttribute(panel_la_kernel<RPL, CPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)panel_stage_bytes<RPL>());
+    if (e != cudaSuccess) return e;
+    configured.mark(dev);
+  }
+  panel_la_kernel<RPL, CPW><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), panel_stage_bytes<RPL>(), s>>>(pp);
+  return cudaGetLastError();
+}
+
+// Panels of 513..1024 rows: one CTA with in-panel look-ahead (default), or QRB200_PANEL=owner
+// for the two-CTA cluster panel.
+static bool panel_lookahead() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_PANEL");
+    v = (e && strcmp(e, "owner") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Panel kernel shape by panel height: panels up to 512 rows are factored by one CTA
-// ("owner computes" form, rows spread over the lanes of each column's warp); taller panels
-// use a cluster of CTAs of 32 warps (one per column): two CTAs of 512 rows up to m = 1024,
-// then ceil(m / 256) CTAs of 256 rows (at most 16).
+// ("owner computes" form, rows spread over the lanes of each column's warp), panels up to
+// 1024 rows by one CTA of 16 warps with in-panel look-ahead; taller panels use a cluster of
+// ceil(m / 256) CTAs of 32 warps (one per column), at most 16.
 static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s, long long t_bstride) {
   PanelParams q = pp;
   q.t_bstride = t_bstride;
   if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
   if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
   if (m <= 512) return launch_owner_cpw<16>(q, batch, s);
+  if (m <= 1024 && panel_lookahead()) return launch_la<32, 2>(q, batch, s);
   if (m <= 1024) return launch_panel<16, true>(q, cdiv(m, 512), batch, s);
   return launch_panel<8, true>(q, cdiv(m, kPanelRows), batch, s);
 }
