@@ -19,6 +19,7 @@
 #include "../../include/qrb200.h"
 #include "panel.cuh"
 #include "panel_la.cuh"
+#include "panel_fw.cuh"
 #include "small.cuh"
 #include "small_fw.cuh"
 #include "wy_simt.cuh"
@@ -314,8 +315,33 @@ static cudaError_t launch_la(const PanelParams& pp, long long batch, cudaStream_
   return cudaGetLastError();
 }
 
+template <int RPL>
+static cudaError_t launch_fw(const PanelParams& pp, long long batch, cudaStream_t s) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
+    cudaError_t e = cudaFuncSetAttribute(panel_fw_kernel<RPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)panel_fw_smem<RPL>());
+    if (e != cudaSuccess) return e;
+    configured.mark(dev);
+  }
+  panel_fw_kernel<RPL><<<dim3(1, (unsigned)batch), 32 * kPanelFwWarps, panel_fw_smem<RPL>(), s>>>(pp);
+  return cudaGetLastError();
+}
+
 // Panels of 513..1024 rows: one CTA with in-panel look-ahead (default), or QRB200_PANEL=owner
 // for the two-CTA cluster panel.
+// QRB200_PANEL_FW=0 keeps the owner-computes panel for panels of up to 512 rows of matrices
+// larger than 512.
+static bool panel_fw() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_PANEL_FW");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static bool panel_lookahead() {
   static int v = -1;
   if (v < 0) {
@@ -332,6 +358,14 @@ static bool panel_lookahead() {
 static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s, long long t_bstride) {
   PanelParams q = pp;
   q.t_bstride = t_bstride;
+  // The factor-warp panel has the shorter chain (latency-bound launches: few, large matrices);
+  // the owner panel fits two CTAs per SM (throughput-bound launches: many small matrices).
+  // The choice depends on the matrix order only, so results stay independent of the batch.
+  if (panel_fw() && pp.n > 512) {
+    if (m <= 128) return launch_fw<4>(q, batch, s);
+    if (m <= 256) return launch_fw<8>(q, batch, s);
+    if (m <= 512) return launch_fw<16>(q, batch, s);
+  }
   if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
   if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
   if (m <= 512) return launch_owner_cpw<16>(q, batch, s);

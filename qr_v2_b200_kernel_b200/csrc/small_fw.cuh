@@ -45,6 +45,17 @@ __device__ __forceinline__ bool fw_wait_geq(const int* p, int v) {
   return false;
 }
 
+// As fw_wait_geq, with a pause between polls (for warps off the critical path that share a
+// scheduler with it); at most 2^20 polls of about 0.1 us.
+__device__ __forceinline__ bool fw_wait_geq_sleep(const int* p, int v) {
+  for (uint32_t it = 0; it < (1u << 20); ++it) {
+    if (ld_acquire_cta(p) >= v) return true;
+    __nanosleep(100);
+  }
+  atomicExch(&g_device_status, kDevStatusHandoffTimeout);
+  return false;
+}
+
 // Publish by lane 0 after every lane's shared-memory writes.
 __device__ __forceinline__ void fw_publish(int* p, int v) {
   __threadfence_block();
@@ -74,7 +85,9 @@ __device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnor
 
 // Factor-warp layout: lane l holds rows l + 32 i (i < RPL) of the block's CPW columns.
 // Factor the block (global columns c0 ..); T (every lane holds all of it), tau written.
-template <int CPW, int RPL>
+// J32: every pivot row is < 32 (a panel of at most 32 columns), so rows 32 i, i >= 1, are
+// always below the pivot and register 0 holds the pivot row.
+template <int CPW, int RPL, bool J32 = false>
 __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int c0, const int n, float (&Tw)[CPW][CPW],
                                                 float* __restrict__ taub) {
   const int lane = threadIdx.x & 31;
@@ -86,10 +99,10 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
   for (int jj = 0; jj < CPW; ++jj) {
     const int j = c0 + jj;
     if (j >= n) break;
-    const int ij = j >> 5, lj = j & 31;
+    const int ij = J32 ? 0 : (j >> 5), lj = j & 31;
     float xm[RPL];
 #pragma unroll
-    for (int i = 0; i < RPL; ++i) xm[i] = (lane + 32 * i > j) ? a[jj][i] : 0.f;
+    for (int i = 0; i < RPL; ++i) xm[i] = ((J32 && i > 0) || lane + 32 * i > j) ? a[jj][i] : 0.f;
     float d[CPW], rowj[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
@@ -98,8 +111,9 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
       for (int i = 0; i < RPL; ++i) acc = fmaf(xm[i], c == jj ? xm[i] : a[c][i], acc);
       d[c] = acc;  // d[jj] = ||x||^2; c > jj: x . a_c; c < jj: x . v_c
       float t = a[c][0];
+      if (!J32)
 #pragma unroll
-      for (int i = 1; i < RPL; ++i) t = (i == ij) ? a[c][i] : t;
+        for (int i = 1; i < RPL; ++i) t = (i == ij) ? a[c][i] : t;
       rowj[c] = t;
     }
 #pragma unroll
@@ -119,7 +133,7 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {
           a[c][i] = fmaf(-fs, xm[i], a[c][i]);
-          if (lane + 32 * i == j) a[c][i] -= f;
+          if ((!J32 || i == 0) && lane + 32 * i == j) a[c][i] -= f;
         }
       }
     }
@@ -134,7 +148,7 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
 #pragma unroll
     for (int i = 0; i < RPL; ++i) {
       const int r = lane + 32 * i;
-      a[jj][i] = (r > j) ? xm[i] * rf.scale : (r == j ? rf.diag : a[jj][i]);
+      a[jj][i] = (J32 && i > 0) ? xm[i] * rf.scale : ((r > j) ? xm[i] * rf.scale : (r == j ? rf.diag : a[jj][i]));
     }
     if (lane == 0) taub[j] = rf.tau;
   }
@@ -195,6 +209,16 @@ __device__ __forceinline__ void fw_apply_cols(float (&a)[CPW][RPL], const float*
     }
 }
 
+// Volatile shared float4 load: issued where it stands, so a long unrolled loop does not hoist
+// all of its loads ahead of the arithmetic (which would need a register per loaded value).
+__device__ __forceinline__ float4 lds4_inorder(const float* p) {
+  float4 v;
+  asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
 // Update-warp layout: lane 4 g + c holds column c, rows 32 q + 4 g + e (q < RPG / 4, e < 4) in
 // x[4 q + e]. The dot products V^T x reduce over the 8 lanes of a column (3 shuffle levels), and
 // the 8 row groups of one float4 load are 8 consecutive 16-byte pieces (no bank conflicts).
@@ -208,7 +232,7 @@ __device__ __forceinline__ void fw_apply_rows(float (&x)[RPG], const float* __re
   for (int k = 0; k < RPG; k += 4) {
 #pragma unroll
     for (int cp = 0; cp < CPW; ++cp) {
-      const float4 v = *reinterpret_cast<const float4*>(Vs + cp * NMAX + 8 * k + g4);
+      const float4 v = lds4_inorder(Vs + cp * NMAX + 8 * k + g4);
       W[cp] = fmaf(v.x, x[k], W[cp]);
       W[cp] = fmaf(v.y, x[k + 1], W[cp]);
       W[cp] = fmaf(v.z, x[k + 2], W[cp]);
@@ -231,7 +255,7 @@ __device__ __forceinline__ void fw_apply_rows(float (&x)[RPG], const float* __re
   for (int k = 0; k < RPG; k += 4) {
 #pragma unroll
     for (int cp = 0; cp < CPW; ++cp) {
-      const float4 v = *reinterpret_cast<const float4*>(Vs + cp * NMAX + 8 * k + g4);
+      const float4 v = lds4_inorder(Vs + cp * NMAX + 8 * k + g4);
       x[k] = fmaf(-v.x, Y[cp], x[k]);
       x[k + 1] = fmaf(-v.y, Y[cp], x[k + 1]);
       x[k + 2] = fmaf(-v.z, Y[cp], x[k + 2]);
