@@ -20,6 +20,7 @@
 #include "panel.cuh"
 #include "panel_la.cuh"
 #include "panel_fw.cuh"
+#include "panel_cl.cuh"
 #include "small.cuh"
 #include "small_fw.cuh"
 #include "wy_simt.cuh"
@@ -329,6 +330,63 @@ static cudaError_t launch_fw(const PanelParams& pp, long long batch, cudaStream_
   return cudaGetLastError();
 }
 
+template <int RPL, bool ASYNC>
+static cudaError_t launch_cl(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
+  static PerDevice configured;
+  const int dev = current_device();
+  if (!configured.done(dev)) {
+    cudaError_t e = cudaFuncSetAttribute(panel_cl_kernel<RPL, ASYNC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)panel_cl_smem<RPL>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(panel_cl_kernel<RPL, ASYNC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured.mark(dev);
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
+  cfg.blockDim = dim3(kClThreads, 1, 1);
+  cfg.dynamicSmemBytes = panel_cl_smem<RPL>();
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, panel_cl_kernel<RPL, ASYNC>, pp);
+}
+
+// Rows per CTA of the cluster panel (QRB200_CL_ROWS = 128, 256 or 512; 0 turns the cluster
+// panel off) and the smallest panel height it takes (QRB200_CL_MIN_M).
+static int cl_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_CL_ROWS");
+    v = e ? atoi(e) : 256;
+    if (v != 0 && v != 128 && v != 256 && v != 512) v = 256;
+  }
+  return v;
+}
+// QRB200_CL_ASYNC=0 exchanges the cluster panel's partials with remote stores and release
+// arrives instead of st.async transactions.
+static bool cl_async() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_CL_ASYNC");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+static int cl_min_m() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_CL_MIN_M");
+    v = e ? atoi(e) : 513;
+  }
+  return v;
+}
+
 // Panels of 513..1024 rows: one CTA with in-panel look-ahead (default), or QRB200_PANEL=owner
 // for the two-CTA cluster panel.
 // QRB200_PANEL_FW=0 keeps the owner-computes panel for panels of up to 512 rows of matrices
@@ -361,6 +419,17 @@ static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batc
   // The factor-warp panel has the shorter chain (latency-bound launches: few, large matrices);
   // the owner panel fits two CTAs per SM (throughput-bound launches: many small matrices).
   // The choice depends on the matrix order only, so results stay independent of the batch.
+  const int clr = cl_rows();
+  if (clr > 0 && m >= cl_min_m() && m <= kClMaxCta * clr) {
+    if (cl_async()) {
+      if (clr == 128) return launch_cl<4, true>(q, cdiv(m, 128), batch, s);
+      if (clr == 512) return launch_cl<16, true>(q, cdiv(m, 512), batch, s);
+      return launch_cl<8, true>(q, cdiv(m, 256), batch, s);
+    }
+    if (clr == 128) return launch_cl<4, false>(q, cdiv(m, 128), batch, s);
+    if (clr == 512) return launch_cl<16, false>(q, cdiv(m, 512), batch, s);
+    return launch_cl<8, false>(q, cdiv(m, 256), batch, s);
+  }
   if (panel_fw() && pp.n > 512) {
     if (m <= 128) return launch_fw<4>(q, batch, s);
     if (m <= 256) return launch_fw<8>(q, batch, s);
