@@ -24,6 +24,8 @@
 #include "small.cuh"
 #include "small_fw.cuh"
 #include "wy_simt.cuh"
+#include "wy_simt2.cuh"
+#include "wy_u1.cuh"
 #include "wy_tc.cuh"
 #include "wy_tc128.cuh"
 
@@ -34,6 +36,7 @@ constexpr int kPanelRows = 256;      // panel rows per CTA of a cluster (32 lane
 constexpr int kMaxCluster = 16;      // non-portable cluster size (one GPC)
 constexpr int kMaxN = kPanelRows * kMaxCluster;        // 4096
 constexpr int kSmallN = 128;         // whole-matrix single-CTA path up to this order
+constexpr int kMaxDevicesSm = 64;
 
 
 // ---------------------------------------------------------------------------------------
@@ -42,12 +45,12 @@ constexpr int kSmallN = 128;         // whole-matrix single-CTA path up to this 
 // records its algorithmic flops and bytes.
 enum KernelKind {
   K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_TC_VTC, K_TC_UPD,
-  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_NUM_KINDS
+  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_U1, K_NUM_KINDS
 };
 static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw", "wy_upd",
                                                    "tc_vtc", "tc_upd", "tc_gram", "tbuild", "tc_ygemm", "tc_vtc128",
-                                                   "tc_upd128"};
-static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1, 1, 0, 1, 1, 1};
+                                                   "tc_upd128", "wy_u1"};
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1, 1, 0, 1, 1, 1, 0};
 
 static std::atomic<long long> g_launches{0};
 
@@ -133,6 +136,17 @@ static bool use_two_level(int n, const float* A, long long abs) {
     v = (e && strcmp(e, "0") == 0) ? 0 : 1;
   }
   return v == 1 && n > kOB && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+}
+
+// Single-level schedule with look-ahead for matrices of order >= QRB200_SINGLE_MIN_N (the
+// choice depends on the order only, so results do not depend on the batch).
+static bool use_single_la(int n) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_SINGLE_MIN_N");
+    v = e ? atoi(e) : 1024;
+  }
+  return n >= v;
 }
 
 static Workspace layout(long long batch, int n, void* base) {
@@ -567,16 +581,61 @@ static cudaError_t tc128_configure() {
   return cudaSuccess;
 }
 
-// Narrow update inside an outer block: columns [k + w, cend) by the panel at k (FP32 cores).
-static cudaError_t launch_narrow(const float* src, long long sbs, float* H, const float* T, const Workspace& ws,
-                                 long long batch, int n, int k, int w, int cend, cudaStream_t s) {
-  const int m = n - k, nc = cend - k - w;
+// QRB200_WY2=0 keeps the first-generation FP32 update kernels for aligned rows too.
+static bool wy2_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_WY2");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// QRB200_WY3=0 keeps the 128-column V^T C tiles and the one-tile-per-CTA update.
+static bool wy3_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_WY3");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Widest update (columns) taken by the one-launch clustered kernel (QRB200_U1_MAX, 0 = off).
+static int u1_max_cols() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_U1_MAX");
+    v = e ? atoi(e) : 128;
+  }
+  return v;
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+static int num_sms() {
+  static int cache[kMaxDevicesSm] = {0};
+  const int dev = current_device();
+  if (dev < kMaxDevicesSm && cache[dev] > 0) return cache[dev];
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+  if (dev < kMaxDevicesSm) cache[dev] = v;
+  return v;
+}
+
+// FP32 compact-WY update of columns [k + w + coff, cend) by the panel at k (the narrow update
+// inside an outer block, or either half of a single-level look-ahead update). T factors sit
+// t_bstride elements apart.
+static cudaError_t launch_wy(const float* src, long long sbs, float* H, const float* T, long long t_bstride,
+                             const Workspace& ws, long long batch, int n, int k, int w, int coff, int cend,
+                             cudaStream_t s, bool allow_u1 = false) {
+  const int m = n - k, nc = cend - k - w, ncl = nc - coff;
+  if (ncl <= 0) return cudaSuccess;
   WyParams wp{};
   wp.src = src;
   wp.src_bstride = sbs;
   wp.H = H;
   wp.T = T;
-  wp.t_bstride = 4 * kNB * kNB;
+  wp.t_bstride = t_bstride;
   wp.Wp = ws.Wp;
   wp.W2 = ws.W2;
   wp.n = n;
@@ -586,18 +645,77 @@ static cudaError_t launch_narrow(const float* src, long long sbs, float* H, cons
   wp.nsplit = choose_nsplit(batch, n, k, w);
   wp.rows_per_split = kRowsPerSplit;
   wp.ncmax = n;
+  wp.coff = coff;
   const double bm = (double)batch * m;
-  {
-    LaunchScope ls(K_VTC, 2.0 * bm * w * nc, 4.0 * bm * (w + nc) + 4.0 * batch * wp.nsplit * w * (double)nc);
-    wy_vtc_kernel<kNB><<<dim3(cdiv(nc, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
+  const bool vec = wy2_enabled() && w == kNB && (n % 4) == 0 && (sbs % 4) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(H)) & 15u) == 0;
+  if (vec) {
+    static PerDevice configured;
+    const int dev = current_device();
+    if (!configured.done(dev)) {
+      cudaError_t e = cudaFuncSetAttribute(wy_vtc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc2Smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_vtc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_upd3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpd3Smem);
+      if (e != cudaSuccess) return e;
+      configured.mark(dev);
+    }
+  }
+  if (allow_u1 && vec && ncl <= u1_max_cols() && m <= kClMaxCta * kU1Rows) {
+    // Short update: one clustered launch (V^T C, T^T and the update together).
+    static PerDevice configured_u1;
+    const int dev = current_device();
+    if (!configured_u1.done(dev)) {
+      cudaError_t e = cudaFuncSetAttribute(wy_u1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kU1Smem);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(wy_u1_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+      configured_u1.mark(dev);
+    }
+    const int cp = cdiv(m, kU1Rows);
+    LaunchScope ls(K_U1, 4.0 * bm * w * ncl + (double)batch * w * w * ncl, 12.0 * bm * ncl + 4.0 * bm * w);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = kU1Smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cp;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, wy_u1_kernel, wp);
+  }
+  if (vec) {
+    LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
+    if (ncl > kV2Cols && wy3_enabled())
+      wy_vtc3_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 256, kVtc3Smem, s>>>(wp);
+    else
+      wy_vtc2_kernel<<<dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), 256, kVtc2Smem, s>>>(wp);
+  } else {
+    LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
+    wy_vtc_kernel<kNB><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
   }
   {
-    LaunchScope ls(K_TW, (double)batch * w * w * nc, 4.0 * batch * (wp.nsplit + 1.0) * w * nc);
-    wy_tw_kernel<kNB><<<dim3(cdiv(nc, 128), (unsigned)batch), 128, 0, s>>>(wp);
+    LaunchScope ls(K_TW, (double)batch * w * w * ncl, 4.0 * batch * (wp.nsplit + 1.0) * w * ncl);
+    if (vec)
+      wy_tw2_kernel<<<dim3(cdiv(ncl, 32), (unsigned)batch), 256, 0, s>>>(wp);
+    else
+      wy_tw_kernel<kNB><<<dim3(cdiv(ncl, 128), (unsigned)batch), 128, 0, s>>>(wp);
   }
   {
-    LaunchScope ls(K_UPD, 2.0 * bm * w * nc, 8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * w * (double)nc);
-    wy_upd_kernel<kNB><<<dim3(cdiv(nc, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
+    LaunchScope ls(K_UPD, 2.0 * bm * w * ncl, 8.0 * bm * ncl + 4.0 * bm * w + 4.0 * batch * w * (double)ncl);
+    if (vec && wy3_enabled()) {
+      const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
+      const long long nt = (long long)tc * tr * batch;
+      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+      wy_upd3_kernel<<<grid, 256, kUpd3Smem, s>>>(wp, tc, tr, (int)nt);
+    } else if (vec)
+      wy_upd2_kernel<<<dim3(cdiv(ncl, kU2Cols), cdiv(m, kU2Rows), (unsigned)batch), 256, 0, s>>>(wp);
+    else
+      wy_upd_kernel<kNB><<<dim3(cdiv(ncl, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
   }
   return cudaGetLastError();
 }
@@ -716,7 +834,7 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
       }
       if (e != cudaSuccess) return e;
       if (kb + w < k0 + ow) {
-        e = launch_narrow(src, sbs, H, Tslot, ws, batch, n, kb, w, k0 + ow, sp);
+        e = launch_wy(src, sbs, H, Tslot, 4 * kNB * kNB, ws, batch, n, kb, w, 0, k0 + ow, sp);
         if (e != cudaSuccess) return e;
       }
     }
@@ -803,6 +921,81 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->pj, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->uj, 0);
   return body != cudaSuccess ? body : e;
+}
+
+// Single-level blocked QR with look-ahead: after panel k (32 columns at kb), U1 updates the
+// next panel's 32 columns on the critical stream sp and U2 everything right of them on su, so
+// U2 of panel k runs while panel k + 1 is factored. U1 of panel k + 1 waits for U2 of panel k
+// (same columns). Panel T factors alternate between two slots of the workspace (U2 of panel k
+// may still read slot k % 2 while panel k + 1 writes the other one); U1 and U2 of one panel use
+// disjoint columns of the partial-product buffers. L == nullptr runs everything on sp.
+static cudaError_t single_level_body(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                     const Workspace& ws, cudaStream_t sp, cudaStream_t su, LookaheadStreams* L) {
+  cudaError_t e;
+  bool u2_pending = false;
+  constexpr long long kTStride = 4 * kNB * kNB;
+  for (int kb = 0; kb < n; kb += kNB) {
+    const int w = std::min(kNB, n - kb), m = n - kb, nc = n - kb - w;
+    const float* src = (kb == 0) ? A : H;
+    const long long sbs = (kb == 0) ? abs : (long long)n * n;
+    float* Tslot = ws.T + (size_t)((kb / kNB) & 1) * kNB * kNB;
+    PanelParams pp{src, sbs, H, tau, nc > 0 ? Tslot : nullptr, n, kb, w};
+    {
+      LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+      e = launch_panel_for(pp, m, batch, sp, kTStride);
+    }
+    if (e != cudaSuccess) return e;
+    if (nc <= 0) continue;
+    if (L == nullptr || nc <= kNB) {
+      // Same two launches as under look-ahead (next panel's columns, then the rest), so both
+      // schedules give bitwise the same result.
+      if (L != nullptr && u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;
+      u2_pending = false;
+      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, std::min(n, kb + w + kNB), sp, true)) !=
+          cudaSuccess)
+        return e;
+      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, n, sp, true)) != cudaSuccess) return e;
+      continue;
+    }
+    if ((e = cudaEventRecord(L->y, sp)) != cudaSuccess) return e;
+    if (u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;  // U2 of panel k - 1
+    if ((e = cudaStreamWaitEvent(su, L->y, 0)) != cudaSuccess) return e;
+    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, n, su, true)) != cudaSuccess) return e;
+    if ((e = cudaEventRecord(L->u2, su)) != cudaSuccess) return e;
+    u2_pending = true;
+    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, kb + w + kNB, sp, true)) != cudaSuccess)
+      return e;
+  }
+  return cudaSuccess;
+}
+
+// Shared fork/join around a look-ahead body: the body runs on the device's two look-ahead
+// streams, both joined back into the caller's stream (also after a failed launch).
+template <class Body>
+static cudaError_t with_lookahead(int dev, cudaStream_t s, Body body) {
+  std::lock_guard<std::mutex> lk(g_la_mu[dev]);
+  LookaheadStreams* L = nullptr;
+  cudaError_t e;
+  if ((e = lookahead_streams(dev, &L)) != cudaSuccess) return e;
+  if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
+  const cudaError_t b = body(L);
+  e = cudaEventRecord(L->pj, L->p);
+  if (e == cudaSuccess) e = cudaEventRecord(L->uj, L->u);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->pj, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->uj, 0);
+  return b != cudaSuccess ? b : e;
+}
+
+static cudaError_t run_single_la(const float* A, float* H, float* tau, long long batch, int n, long long abs,
+                                 const Workspace& ws, cudaStream_t s) {
+  const int dev = current_device();
+  if (t_prof || !lookahead_enabled() || n <= 2 * kNB || dev >= kMaxDevices)
+    return single_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
+  return with_lookahead(dev, s, [&](LookaheadStreams* L) {
+    return single_level_body(A, H, tau, batch, n, abs, ws, L->p, L->u, L);
+  });
 }
 
 }  // namespace qrb200
@@ -895,8 +1088,12 @@ static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64
     const Workspace ws = layout(batch, (int)n, workspace);
     if (workspace_bytes < ws.bytes || !workspace) return QRB200_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return QRB200_ERR_WORKSPACE;
-    e = use_two_level((int)n, A, a_batch_stride) ? run_two_level(A, H, tau, batch, (int)n, a_batch_stride, ws, s)
-                                                   : run_blocked(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
+    if (use_single_la((int)n) && !use_tc_update((int)n, A, a_batch_stride))
+      e = run_single_la(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
+    else if (use_two_level((int)n, A, a_batch_stride))
+      e = run_two_level(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
+    else
+      e = run_blocked(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
   }
   if (e != cudaSuccess) return QRB200_ERR_CUDA;
   return QRB200_OK;

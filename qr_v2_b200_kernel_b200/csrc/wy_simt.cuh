@@ -28,7 +28,8 @@ struct WyParams {
   int nsplit;             // row splits of the V^T C product
   int rows_per_split;     // multiple of 32
   int ncmax;              // leading dimension of Wp / W2 (>= cend - k - w)
-  int coff;               // 128-wide kernels: first trailing column (relative to k + w) of this launch
+  int coff;               // first trailing column (relative to k + w) of this launch (tile-aligned
+                          // for the 128-wide kernels)
 };
 
 // V[r][c] of the panel starting at (k, k): unit lower trapezoid stored in H.
@@ -46,7 +47,7 @@ __global__ void __launch_bounds__(256) wy_vtc_kernel(WyParams P) {
   __shared__ float Cs[32][64 + 1];
   const int bidx = blockIdx.z, split = blockIdx.y;
   const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
-  const int col0 = blockIdx.x * 64;
+  const int col0 = P.coff + blockIdx.x * 64;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   const int tid = threadIdx.x;
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(128) wy_tw_kernel(WyParams P) {
   const float* Tb = P.T + (long long)bidx * P.t_bstride;
   for (int e = threadIdx.x; e < NB * NB; e += blockDim.x) Ts[e / NB][e % NB] = Tb[e];
   __syncthreads();
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = P.coff + blockIdx.x * blockDim.x + threadIdx.x;
   if (col >= nc) return;
   float wv[NB];
 #pragma unroll
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(256) wy_upd_kernel(WyParams P) {
   __shared__ float Ws[NB][64 + 4];
   const int bidx = blockIdx.z;
   const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
-  const int row0 = blockIdx.y * 64, col0 = blockIdx.x * 64;
+  const int row0 = blockIdx.y * 64, col0 = P.coff + blockIdx.x * 64;
   const float* __restrict__ Hb_in = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Hb = P.H + (long long)bidx * n * n;

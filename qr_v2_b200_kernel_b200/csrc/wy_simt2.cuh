@@ -1,0 +1,433 @@
+// Streaming FP32 kernels for the 32-wide compact-WY update C <- C - V T^T V^T C
+// (milestones/01_eager_official123203us.py:102-107, submission.py:453-480), for rows whose
+// starts are 16-byte aligned (n % 4 == 0 and a 16-byte aligned batch):
+//
+//   wy_vtc2_kernel : Wp[s] = V_s^T C_s  over a row split s; 32 x 128 outputs per CTA, the rows
+//                    streamed in 32-row stages by cp.async (three stages in flight), 4 x 4
+//                    outputs per thread;
+//   wy_upd2_kernel : C <- C - V W2 on a 128 x 64 tile, K = 32: V (transposed) and W2 staged in
+//                    shared memory while each thread's 8 x 4 slice of C is already on its way
+//                    into registers.
+// The T^T product between them is wy_tw_kernel. Same arithmetic per output as wy_simt.cuh
+// except for the summation order inside each partial product.
+#pragma once
+
+#include "common.cuh"
+#include "tc.cuh"
+#include "wy_simt.cuh"
+
+namespace qrb200 {
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kV2Cols = 128, kV2Rows = 32, kV2Stages = 3;
+struct Vtc2Stage {
+  float C[kV2Rows][kV2Cols];
+  float V[kV2Rows][32];
+};
+constexpr size_t kVtc2Smem = sizeof(Vtc2Stage) * kV2Stages;
+
+__global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
+  extern __shared__ __align__(16) unsigned char v2_smem_raw[];
+  Vtc2Stage* st = reinterpret_cast<Vtc2Stage*>(v2_smem_raw);
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
+  const int col0 = P.coff + blockIdx.x * kV2Cols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int tid = threadIdx.x, tx = tid & 31, ty = tid >> 5;
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(n - k, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV2Rows - 1) / kV2Rows : 0;
+
+  auto issue = [&](int ch) {
+    Vtc2Stage& s = st[ch % kV2Stages];
+    const int rb = r_begin + ch * kV2Rows;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {  // C: 32 rows x 32 float4
+      const int e = it * 256 + tid, rr = e >> 5, q = e & 31, r = rb + rr, col = col0 + 4 * q;
+      const bool ok = r < r_end && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+    {  // V: 32 rows x 8 float4
+      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
+      const bool ok = r < r_end && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+  };
+
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+#pragma unroll
+  for (int s = 0; s < kV2Stages - 1; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit();
+  }
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<kV2Stages - 2>();
+    __syncthreads();
+    if (ch + kV2Stages - 1 < nchunks) issue(ch + kV2Stages - 1);
+    cp_async_commit();
+    Vtc2Stage& s = st[ch % kV2Stages];
+    if (split == 0 && ch == 0) {
+      // Rows 0..31 of the panel: V is unit lower triangular there (R sits above the diagonal).
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int e = it * 256 + tid, rr = e >> 5, c = e & 31;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+#pragma unroll 8
+    for (int rr = 0; rr < kV2Rows; ++rr) {
+      const float4 v = *reinterpret_cast<const float4*>(&s.V[rr][4 * ty]);
+      const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * tx]);
+      const float vv[4] = {v.x, v.y, v.z, v.w}, cc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], cc[e], acc[i][e]);
+    }
+  }
+  cp_async_wait<0>();
+  const int col = col0 + 4 * tx;
+  if (col < nc) {
+    float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4*>(out + (long long)(4 * ty + i) * P.ncmax + col) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  }
+}
+
+constexpr int kU2Rows = 128, kU2Cols = 64;
+struct Upd2Shared {
+  float Vt[32][kU2Rows + 4];  // V transposed: Vt[c][r]
+  float W[32][kU2Cols];
+};
+
+__global__ void __launch_bounds__(256) wy_upd2_kernel(WyParams P) {
+  __shared__ __align__(16) Upd2Shared sh;
+  const int bidx = blockIdx.z;
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
+  const int row0 = blockIdx.y * kU2Rows, col0 = P.coff + blockIdx.x * kU2Cols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  float* __restrict__ Ho = P.H + (long long)bidx * n * n;
+  const float* __restrict__ W2b = P.W2 + (long long)bidx * 32 * P.ncmax;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int col = col0 + 4 * tx;
+  const bool col_ok = col < nc;
+  // This thread's C slice (rows row0 + 8 ty .. +7, columns col .. col+3), requested first.
+  float4 cv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = row0 + 8 * ty + i;
+    cv[i] = (r < m && col_ok) ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + col)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // V tile (128 x 32, masked unit lower trapezoid) transposed into shared memory.
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = row0 + rr, c = 4 * q;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < m && c < w) v = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
+    float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e2 = 0; e2 < 4; ++e2) vv[e2] = (c + e2 >= w) ? 0.f : (r > c + e2 ? vv[e2] : (r == c + e2 ? 1.f : 0.f));
+#pragma unroll
+    for (int e2 = 0; e2 < 4; ++e2) sh.Vt[c + e2][rr] = vv[e2];
+  }
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int e = it * 256 + tid, c = e >> 4, q = e & 15, cl = col0 + 4 * q;
+    *reinterpret_cast<float4*>(&sh.W[c][4 * q]) =
+        (cl < nc) ? *reinterpret_cast<const float4*>(W2b + (long long)c * P.ncmax + cl) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+#pragma unroll 8
+  for (int c = 0; c < 32; ++c) {
+    const float4 v0 = *reinterpret_cast<const float4*>(&sh.Vt[c][8 * ty]);
+    const float4 v1 = *reinterpret_cast<const float4*>(&sh.Vt[c][8 * ty + 4]);
+    const float4 x = *reinterpret_cast<const float4*>(&sh.W[c][4 * tx]);
+    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w}, xx[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], xx[e], acc[i][e]);
+  }
+  if (!col_ok) return;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = row0 + 8 * ty + i;
+    if (r < m)
+      *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
+          make_float4(cv[i].x - acc[i][0], cv[i].y - acc[i][1], cv[i].z - acc[i][2], cv[i].w - acc[i][3]);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Wide-tile V^T C: 32 x 256 outputs per CTA (8 x 4 per thread: the eight V columns of a warp
+// are one broadcast read, the four C columns one conflict-free float4), rows streamed in
+// 16-row stages, four stages in flight.
+constexpr int kV3Cols = 256, kV3Rows = 16, kV3Stages = 4;
+struct Vtc3Stage {
+  float C[kV3Rows][kV3Cols];
+  float V[kV3Rows][32];
+};
+constexpr size_t kVtc3Smem = sizeof(Vtc3Stage) * kV3Stages;
+
+__global__ void __launch_bounds__(256) wy_vtc3_kernel(WyParams P) {
+  extern __shared__ __align__(16) unsigned char v3_smem_raw[];
+  Vtc3Stage* st = reinterpret_cast<Vtc3Stage*>(v3_smem_raw);
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
+  const int col0 = P.coff + blockIdx.x * kV3Cols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int tid = threadIdx.x, cg = tid & 63, rg = tid >> 6;
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(n - k, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV3Rows - 1) / kV3Rows : 0;
+
+  auto issue = [&](int ch) {
+    Vtc3Stage& s = st[ch % kV3Stages];
+    const int rb = r_begin + ch * kV3Rows;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {  // C: 16 rows x 64 float4
+      const int e = it * 256 + tid, rr = e >> 6, q = e & 63, r = rb + rr, col = col0 + 4 * q;
+      const bool ok = r < r_end && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+    if (tid < 128) {  // V: 16 rows x 8 float4
+      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
+      const bool ok = r < r_end && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+  };
+
+  // acc[ip][e] holds W rows 8 rg + 2 ip and 8 rg + 2 ip + 1 of column 4 cg + e (paired FMAs).
+  float2 acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kV3Stages - 1; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit();
+  }
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<kV3Stages - 2>();
+    __syncthreads();
+    if (ch + kV3Stages - 1 < nchunks) issue(ch + kV3Stages - 1);
+    cp_async_commit();
+    Vtc3Stage& s = st[ch % kV3Stages];
+    if (split == 0 && ch < 2) {
+      // Panel rows 0..31 (the first two stages): V is unit lower triangular there.
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {
+        const int e = it * 256 + tid, rr = e >> 5, c = e & 31, r = ch * kV3Rows + rr;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (r > c ? v : (r == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int rr = 0; rr < kV3Rows; ++rr) {
+      const float4 v0 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg]);
+      const float4 v1 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg + 4]);
+      const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * cg]);
+      const float2 vp[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w), make_float2(v1.x, v1.y),
+                            make_float2(v1.z, v1.w)};
+      const float cc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 ce = make_float2(cc[e], cc[e]);
+#pragma unroll
+        for (int ip = 0; ip < 4; ++ip) acc[ip][e] = __ffma2_rn(vp[ip], ce, acc[ip][e]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  const int col = col0 + 4 * cg;
+  if (col < nc) {
+    float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
+#pragma unroll
+    for (int ip = 0; ip < 4; ++ip) {
+      *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip) * P.ncmax + col) =
+          make_float4(acc[ip][0].x, acc[ip][1].x, acc[ip][2].x, acc[ip][3].x);
+      *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip + 1) * P.ncmax + col) =
+          make_float4(acc[ip][0].y, acc[ip][1].y, acc[ip][2].y, acc[ip][3].y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Persistent C <- C - V W2 over 64 x 64 tiles: each CTA walks tiles blockIdx.x, + gridDim.x,
+// ..., with the next tile's C, V and W2 slices already streaming into the other half of a
+// two-stage cp.async ring while the current one is computed (4 x 4 outputs per thread; three
+// CTAs per SM).
+constexpr int kU3Rows = 64, kU3Cols = 64;
+struct Upd3Stage {
+  float C[kU3Rows][kU3Cols];
+  float V[kU3Rows][32 + 4];
+  float W[32][kU3Cols];
+};
+constexpr size_t kUpd3Smem = sizeof(Upd3Stage) * 2;
+
+__global__ void __launch_bounds__(256) wy_upd3_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+  extern __shared__ __align__(16) unsigned char u3_smem_raw[];
+  Upd3Stage* st = reinterpret_cast<Upd3Stage*>(u3_smem_raw);
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
+  const int tid = threadIdx.x, cg = tid & 15, rg = tid >> 4;
+  auto tile_of = [&](int t, int& b, int& row0, int& col0) {
+    const int per_b = tiles_c * tiles_r;
+    b = t / per_b;
+    const int rem = t - b * per_b;
+    row0 = (rem / tiles_c) * kU3Rows;
+    col0 = P.coff + (rem % tiles_c) * kU3Cols;
+  };
+  auto issue = [&](int t, int slot) {
+    int b, row0, col0;
+    tile_of(t, b, row0, col0);
+    Upd3Stage& s = st[slot];
+    const float* __restrict__ Sb = P.src + (long long)b * P.src_bstride;
+    const float* __restrict__ Hb = P.H + (long long)b * n * n;
+    const float* __restrict__ W2b = P.W2 + (long long)b * 32 * P.ncmax;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {  // C: 64 rows x 16 float4
+      const int e = it * 256 + tid, rr = e >> 4, q = e & 15, r = row0 + rr, col = col0 + 4 * q;
+      const bool ok = r < m && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {  // V: 64 rows x 8 float4
+      const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = row0 + rr;
+      const bool ok = r < m && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {  // W2: 32 rows x 16 float4
+      const int e = it * 256 + tid, c = e >> 4, q = e & 15, col = col0 + 4 * q;
+      const bool ok = col < nc;
+      cp_async16(&s.W[c][4 * q], ok ? W2b + (long long)c * P.ncmax + col : W2b, ok);
+    }
+  };
+  int t = blockIdx.x;
+  if (t < ntiles) issue(t, 0);
+  cp_async_commit();
+  for (int it = 0; t < ntiles; t += gridDim.x, ++it) {
+    const int slot = it & 1;
+    const int tn = t + gridDim.x;
+    if (tn < ntiles) issue(tn, slot ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    int b, row0, col0;
+    tile_of(t, b, row0, col0);
+    Upd3Stage& s = st[slot];
+    if (row0 == 0) {
+      // Panel rows 0..31: V is unit lower triangular there.
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int e = q * 256 + tid, rr = e >> 5, c = e & 31;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+    // acc[i][h] holds columns 4 cg + 2 h, 4 cg + 2 h + 1 of row 4 rg + i (paired FMAs).
+    float2 acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+#pragma unroll 2
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      float4 vr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vr[i] = *reinterpret_cast<const float4*>(&s.V[4 * rg + i][c4]);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float4 x = *reinterpret_cast<const float4*>(&s.W[c4 + cc][4 * cg]);
+        const float2 x0 = make_float2(x.x, x.y), x1 = make_float2(x.z, x.w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float v = cc == 0 ? vr[i].x : (cc == 1 ? vr[i].y : (cc == 2 ? vr[i].z : vr[i].w));
+          const float2 vv = make_float2(v, v);
+          acc[i][0] = __ffma2_rn(vv, x0, acc[i][0]);
+          acc[i][1] = __ffma2_rn(vv, x1, acc[i][1]);
+        }
+      }
+    }
+    const int col = col0 + 4 * cg;
+    if (col < nc) {
+      float* __restrict__ Ho = P.H + (long long)b * n * n;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = row0 + 4 * rg + i;
+        if (r < m) {
+          const float4 c = *reinterpret_cast<const float4*>(&s.C[4 * rg + i][4 * cg]);
+          *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
+              make_float4(c.x - acc[i][0].x, c.y - acc[i][0].y, c.z - acc[i][1].x, c.w - acc[i][1].y);
+        }
+      }
+    }
+    __syncthreads();  // the slot is refilled by the next iteration's issue
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------------------
+// W2 = T^T sum_s Wp[s] for 32 columns per CTA: thread (row group g, column c) adds the row-split
+// partials of W rows 4 g .. 4 g + 3 (independent, coalesced loads), then forms the same rows
+// of T^T W from shared memory.
+__global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
+  __shared__ float Ts[32][33];
+  __shared__ float Ws[32][33];
+  const int bidx = blockIdx.y;
+  const int nc = P.cend - P.k - P.w;
+  const int tid = threadIdx.x, c = tid & 31, g = tid >> 5;
+  const int col = P.coff + blockIdx.x * 32 + c;
+  const float* Tb = P.T + (long long)bidx * P.t_bstride;
+  for (int e = tid; e < 32 * 32; e += 256) Ts[e >> 5][e & 31] = Tb[e];
+  float wv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (col < nc) {
+    for (int s = 0; s < P.nsplit; ++s) {
+      const float* Wb = P.Wp + ((long long)bidx * P.nsplit + s) * 32 * P.ncmax;
+#pragma unroll
+      for (int a = 0; a < 4; ++a) wv[a] += Wb[(long long)(4 * g + a) * P.ncmax + col];
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) Ws[4 * g + a][c] = wv[a];
+  __syncthreads();
+  if (col >= nc) return;
+  float* out = P.W2 + (long long)bidx * 32 * P.ncmax;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int i = 4 * g + a;
+    float acc = 0.f;
+    for (int cc = 0; cc <= i; ++cc) acc = fmaf(Ts[cc][i], Ws[cc][c], acc);
+    out[(long long)i * P.ncmax + col] = acc;
+  }
+}
+
+}  // namespace qrb200

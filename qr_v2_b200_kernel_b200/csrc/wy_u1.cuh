@@ -1,0 +1,181 @@
+// One-launch compact-WY update of a few trailing columns by a 32-wide panel,
+// C <- C - V T^T V^T C (milestones/01_eager_official123203us.py:102-107), for the short
+// updates that sit on the critical path: the next panel's columns under look-ahead, or the
+// narrow updates inside an outer block. Rows must start on 16-byte boundaries.
+//
+// A thread-block cluster of CP CTAs covers the m rows (256 per CTA); blockIdx.y picks a
+// 32-column slice of C, blockIdx.z the matrix. Each CTA
+//   (1) stages its rows of V (unit lower trapezoid, masked) and of the C slice in shared memory
+//       with coalesced 16-byte loads,
+//   (2) forms its partial W_p = V_p^T C_p (32 x 32; each thread a 4 x 4 block over a quarter
+//       of the rows, the quarters added in shared memory),
+//   (3) after one cluster barrier adds the CP partials from the peers' shared memory in rank
+//       order (every CTA gets bitwise the same W) and forms W2 = T^T W,
+//   (4) writes C_p - V_p W2 back (one row per thread, stored through shared memory).
+// A second cluster barrier keeps every CTA's partial readable until all peers are done.
+#pragma once
+
+#include "common.cuh"
+#include "panel_cl.cuh"
+#include "tc.cuh"
+#include "wy_simt.cuh"
+
+namespace qrb200 {
+
+constexpr int kU1Rows = 256, kU1Ld = 36;
+
+struct __align__(16) U1Shared {
+  float V[kU1Rows][kU1Ld];
+  float C[kU1Rows][kU1Ld];
+  float Wq[4][32][32];  // row-quarter partials
+  float W[32][32];      // this CTA's partial V^T C, read by the peers
+  float Wt[32][33];     // the cluster total
+  float W2[32][32];     // T^T W
+  float T[32][33];
+};
+constexpr size_t kU1Smem = sizeof(U1Shared);
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float x;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(addr) : "memory");
+  return x;
+}
+
+__global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
+  extern __shared__ __align__(16) unsigned char u1_smem_raw[];
+  U1Shared& sh = *reinterpret_cast<U1Shared*>(u1_smem_raw);
+  uint32_t CP, p;
+  asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(CP));
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(p));
+  const int bidx = blockIdx.z;
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
+  const int c0 = P.coff + blockIdx.y * 32;  // first trailing column of this slice
+  const int r0 = (int)p * kU1Rows;
+  const int tid = threadIdx.x;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  float* __restrict__ Ho = P.H + (long long)bidx * n * n;
+
+  // (1) stage V and C (8 threads per row, 16 bytes each).
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), x = v;
+    if (r < m) {
+      if (c < w) v = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
+      if (c0 + c < nc) x = *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + c0 + c);
+    }
+    if (r < 32) {  // unit lower triangle at the top of the panel
+      v.x = (c >= w) ? 0.f : (r > c ? v.x : (r == c ? 1.f : 0.f));
+      v.y = (c + 1 >= w) ? 0.f : (r > c + 1 ? v.y : (r == c + 1 ? 1.f : 0.f));
+      v.z = (c + 2 >= w) ? 0.f : (r > c + 2 ? v.z : (r == c + 2 ? 1.f : 0.f));
+      v.w = (c + 3 >= w) ? 0.f : (r > c + 3 ? v.w : (r == c + 3 ? 1.f : 0.f));
+    }
+    *reinterpret_cast<float4*>(&sh.V[rr][c]) = v;
+    *reinterpret_cast<float4*>(&sh.C[rr][c]) = x;
+  }
+  for (int e = tid; e < 32 * 32; e += 256) sh.T[e >> 5][e & 31] = P.T[(long long)bidx * P.t_bstride + e];
+  __syncthreads();
+  // (2) partial W over the slab: thread (rq, ig, cg) sums rows rq, rq + 4, ... for a 4 x 4 block.
+  {
+    const int cg = tid & 7, ig = (tid >> 3) & 7, rq = tid >> 6;
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+#pragma unroll 4
+    for (int r = rq; r < kU1Rows; r += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(&sh.V[r][4 * ig]);
+      const float4 x = *reinterpret_cast<const float4*>(&sh.C[r][4 * cg]);
+      const float vv[4] = {v.x, v.y, v.z, v.w}, xx[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(vv[a], xx[b], acc[a][b]);
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+      *reinterpret_cast<float4*>(&sh.Wq[rq][4 * ig + a][4 * cg]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+  }
+  __syncthreads();
+  const int i = tid >> 3, cq = tid & 7;
+  {
+    float4 s = *reinterpret_cast<const float4*>(&sh.Wq[0][i][4 * cq]);
+#pragma unroll
+    for (int q = 1; q < 4; ++q) {
+      const float4 t = *reinterpret_cast<const float4*>(&sh.Wq[q][i][4 * cq]);
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+    *reinterpret_cast<float4*>(&sh.W[i][4 * cq]) = s;
+  }
+  // (3) cluster total in rank order, then W2 = T^T W.
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  {
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t q = 0; q < CP; ++q) {
+      const uint32_t base = cl_map(&sh.W[i][4 * cq], q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tot[e] += ld_cluster_f32(base + 4u * e);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sh.Wt[i][4 * cq + e] = tot[e];
+  }
+  __syncthreads();
+  {
+    float y[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c <= i; ++c) {
+      const float t = sh.T[c][i];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) y[e] = fmaf(t, sh.Wt[c][4 * cq + e], y[e]);
+    }
+    *reinterpret_cast<float4*>(&sh.W2[i][4 * cq]) = make_float4(y[0], y[1], y[2], y[3]);
+  }
+  __syncthreads();
+  // (4) C_p - V_p W2, one row per thread, back through shared memory.
+  {
+    float out[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 x = *reinterpret_cast<const float4*>(&sh.C[tid][4 * q]);
+      out[4 * q] = x.x;
+      out[4 * q + 1] = x.y;
+      out[4 * q + 2] = x.z;
+      out[4 * q + 3] = x.w;
+    }
+#pragma unroll 2
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(&sh.V[tid][c4]);
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 y = *reinterpret_cast<const float4*>(&sh.W2[c4 + a][4 * q]);
+          out[4 * q] = fmaf(-vv[a], y.x, out[4 * q]);
+          out[4 * q + 1] = fmaf(-vv[a], y.y, out[4 * q + 1]);
+          out[4 * q + 2] = fmaf(-vv[a], y.z, out[4 * q + 2]);
+          out[4 * q + 3] = fmaf(-vv[a], y.w, out[4 * q + 3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4*>(&sh.C[tid][4 * q]) = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
+    if (r < m && c0 + c < nc)
+      *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + c0 + c) =
+          *reinterpret_cast<const float4*>(&sh.C[rr][c]);
+  }
+  // No CTA leaves while a peer may still read its partial.
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+}  // namespace qrb200

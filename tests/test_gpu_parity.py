@@ -162,10 +162,11 @@ def _profiled(A):
     return H, tau
 
 
-@pytest.mark.parametrize("batch,n", [(3, 384), (4, 512), (2, 1000), (2, 1024)])
+@pytest.mark.parametrize("batch,n", [(3, 384), (4, 512), (2, 1000), (2, 1024), (1, 1536)])
 def test_lookahead_schedule_matches_serial_schedule(batch, n):
-    # The look-ahead cuts each wide update at a 128-column tile boundary and runs part of it
-    # on a second stream; every column still sees the same tiles, so results agree bit for bit.
+    # The look-ahead cuts each update (128-column tiles of the two-level schedule; the next
+    # panel's 32 columns of the single-level schedule, n >= 1024) and runs part of it on a
+    # second stream; the serial schedule makes the same cuts, so results agree bit for bit.
     A = torch.randn(batch, n, n, device="cuda")
     H, tau = _run(A)
     Hs, taus = _profiled(A)
