@@ -410,11 +410,25 @@ __global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
   for (int e = tid; e < 32 * 32; e += 256) Ts[e >> 5][e & 31] = Tb[e];
   float wv[4] = {0.f, 0.f, 0.f, 0.f};
   if (col < nc) {
-    for (int s = 0; s < P.nsplit; ++s) {
-      const float* Wb = P.Wp + ((long long)bidx * P.nsplit + s) * 32 * P.ncmax;
+    // Splits in groups of four: sixteen independent loads in flight before the adds (which
+    // keep the split order).
+    const float* W0 = P.Wp + (long long)bidx * P.nsplit * 32 * P.ncmax + (long long)(4 * g) * P.ncmax + col;
+    const long long sstride = 32LL * P.ncmax;
+    int s = 0;
+    for (; s + 4 <= P.nsplit; s += 4) {
+      float x[4][4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) wv[a] += Wb[(long long)(4 * g + a) * P.ncmax + col];
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int a = 0; a < 4; ++a) x[u][a] = W0[(s + u) * sstride + (long long)a * P.ncmax];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int a = 0; a < 4; ++a) wv[a] += x[u][a];
     }
+    for (; s < P.nsplit; ++s)
+#pragma unroll
+      for (int a = 0; a < 4; ++a) wv[a] += W0[s * sstride + (long long)a * P.ncmax];
   }
 #pragma unroll
   for (int a = 0; a < 4; ++a) Ws[4 * g + a][c] = wv[a];

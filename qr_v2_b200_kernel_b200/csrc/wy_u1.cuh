@@ -35,9 +35,11 @@ struct __align__(16) U1Shared {
 };
 constexpr size_t kU1Smem = sizeof(U1Shared);
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float x;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(addr) : "memory");
+// Peer shared-memory load (the cluster barrier before it orders the peer's writes); not
+// volatile, so independent loads are issued back to back.
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 x;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w) : "r"(addr));
   return x;
 }
 
@@ -115,14 +117,22 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
   // (3) cluster total in rank order, then W2 = T^T W.
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   {
-    float tot[4] = {0.f, 0.f, 0.f, 0.f};
-    for (uint32_t q = 0; q < CP; ++q) {
-      const uint32_t base = cl_map(&sh.W[i][4 * cq], q);
+    float4 part[kClMaxCta];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) tot[e] += ld_cluster_f32(base + 4u * e);
+    for (int q = 0; q < kClMaxCta; ++q)
+      part[q] = (q < (int)CP) ? ld_cluster_f4(cl_map(&sh.W[i][4 * cq], (uint32_t)q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 tot = part[0];
+#pragma unroll
+    for (int q = 1; q < kClMaxCta; ++q) {
+      tot.x += part[q].x;
+      tot.y += part[q].y;
+      tot.z += part[q].z;
+      tot.w += part[q].w;
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) sh.Wt[i][4 * cq + e] = tot[e];
+    sh.Wt[i][4 * cq] = tot.x;
+    sh.Wt[i][4 * cq + 1] = tot.y;
+    sh.Wt[i][4 * cq + 2] = tot.z;
+    sh.Wt[i][4 * cq + 3] = tot.w;
   }
   __syncthreads();
   {
