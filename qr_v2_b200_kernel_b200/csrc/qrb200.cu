@@ -611,6 +611,26 @@ static int u1_max_cols() {
   return v;
 }
 
+// QRB200_WY4=0 keeps the 64 x 64 update tiles for updates wider than 64 columns.
+static bool wy4_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_WY4");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+// QRB200_VTC8X8=1 selects the 8 x 8-per-thread V^T C kernel (measured slower on B200 than the
+// 8 x 4 one at C3 and C5, so off by default).
+static bool wy_vtc8x8() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_VTC8X8");
+    v = (e && strcmp(e, "1") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
 // Streaming multiprocessors of the current device (cached per device).
 static int num_sms() {
   static int cache[kMaxDevicesSm] = {0};
@@ -658,6 +678,10 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
         e = cudaFuncSetAttribute(wy_vtc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_upd3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpd3Smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_vtc4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_upd4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpd4Smem);
       if (e != cudaSuccess) return e;
       configured.mark(dev);
     }
@@ -691,7 +715,12 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   if (vec) {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
     if (ncl > kV2Cols && wy3_enabled())
-      wy_vtc3_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 256, kVtc3Smem, s>>>(wp);
+    {
+      if (wy_vtc8x8())
+        wy_vtc4_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 128, kVtc3Smem, s>>>(wp);
+      else
+        wy_vtc3_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 256, kVtc3Smem, s>>>(wp);
+    }
     else
       wy_vtc2_kernel<<<dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), 256, kVtc2Smem, s>>>(wp);
   } else {
@@ -707,7 +736,12 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   }
   {
     LaunchScope ls(K_UPD, 2.0 * bm * w * ncl, 8.0 * bm * ncl + 4.0 * bm * w + 4.0 * batch * w * (double)ncl);
-    if (vec && wy3_enabled()) {
+    if (vec && wy3_enabled() && wy4_enabled() && ncl > kU3Cols) {
+      const int tc = cdiv(ncl, kU4Cols), tr = cdiv(m, kU4Rows);
+      const long long nt = (long long)tc * tr * batch;
+      const int grid = (int)std::min<long long>(nt, 2LL * num_sms());
+      wy_upd4_kernel<<<grid, 256, kUpd4Smem, s>>>(wp, tc, tr, (int)nt);
+    } else if (vec && wy3_enabled()) {
       const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
       const long long nt = (long long)tc * tr * batch;
       const int grid = (int)std::min<long long>(nt, 3LL * num_sms());

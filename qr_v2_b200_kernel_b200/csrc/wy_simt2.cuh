@@ -444,4 +444,221 @@ __global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// V^T C with 8 x 8 outputs per thread (128 threads, 32 x 256 outputs per CTA): per row, two
+// broadcast float4 reads of V and two contiguous float4 reads of C (columns 4 cg .. and
+// 128 + 4 cg ..) feed 64 FMAs, so shared memory is no longer the limiter. Same stages as
+// wy_vtc3_kernel.
+__global__ void __launch_bounds__(128) wy_vtc4_kernel(WyParams P) {
+  extern __shared__ __align__(16) unsigned char v4_smem_raw[];
+  Vtc3Stage* st = reinterpret_cast<Vtc3Stage*>(v4_smem_raw);
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
+  const int col0 = P.coff + blockIdx.x * kV3Cols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int tid = threadIdx.x, cg = tid & 31, rg = tid >> 5;
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(n - k, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV3Rows - 1) / kV3Rows : 0;
+
+  auto issue = [&](int ch) {
+    Vtc3Stage& s = st[ch % kV3Stages];
+    const int rb = r_begin + ch * kV3Rows;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {  // C: 16 rows x 64 float4
+      const int e = it * 128 + tid, rr = e >> 6, q = e & 63, r = rb + rr, col = col0 + 4 * q;
+      const bool ok = r < r_end && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+    {  // V: 16 rows x 8 float4
+      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
+      const bool ok = r < r_end && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+  };
+
+  // acc[ip][e]: W rows 8 rg + 2 ip, + 1 of column e of this thread's eight
+  // (e < 4: 4 cg + e; e >= 4: 128 + 4 cg + e - 4).
+  float2 acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[i][e] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kV3Stages - 1; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit();
+  }
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<kV3Stages - 2>();
+    __syncthreads();
+    if (ch + kV3Stages - 1 < nchunks) issue(ch + kV3Stages - 1);
+    cp_async_commit();
+    Vtc3Stage& s = st[ch % kV3Stages];
+    if (split == 0 && ch < 2) {
+      // Panel rows 0..31 (the first two stages): V is unit lower triangular there.
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int e = it * 128 + tid, rr = e >> 5, c = e & 31, r = ch * kV3Rows + rr;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (r > c ? v : (r == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+#pragma unroll 4
+    for (int rr = 0; rr < kV3Rows; ++rr) {
+      const float4 v0 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg]);
+      const float4 v1 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg + 4]);
+      const float4 c0 = *reinterpret_cast<const float4*>(&s.C[rr][4 * cg]);
+      const float4 c1 = *reinterpret_cast<const float4*>(&s.C[rr][128 + 4 * cg]);
+      const float2 vp[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w), make_float2(v1.x, v1.y),
+                            make_float2(v1.z, v1.w)};
+      const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float2 ce = make_float2(cc[e], cc[e]);
+#pragma unroll
+        for (int ip = 0; ip < 4; ++ip) acc[ip][e] = __ffma2_rn(vp[ip], ce, acc[ip][e]);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int col = col0 + 128 * h + 4 * cg;
+    if (col < nc) {
+#pragma unroll
+      for (int ip = 0; ip < 4; ++ip) {
+        *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip) * P.ncmax + col) =
+            make_float4(acc[ip][4 * h].x, acc[ip][4 * h + 1].x, acc[ip][4 * h + 2].x, acc[ip][4 * h + 3].x);
+        *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip + 1) * P.ncmax + col) =
+            make_float4(acc[ip][4 * h].y, acc[ip][4 * h + 1].y, acc[ip][4 * h + 2].y, acc[ip][4 * h + 3].y);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Persistent C <- C - V W2 over 64 x 128 tiles (4 x 8 outputs per thread: columns 4 cg .. and
+// 64 + 4 cg ..), same two-stage cp.async ring as wy_upd3_kernel; two CTAs per SM.
+constexpr int kU4Rows = 64, kU4Cols = 128;
+struct Upd4Stage {
+  float C[kU4Rows][kU4Cols];
+  float V[kU4Rows][32];
+  float W[32][kU4Cols];
+};
+constexpr size_t kUpd4Smem = sizeof(Upd4Stage) * 2;
+
+__global__ void __launch_bounds__(256) wy_upd4_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+  extern __shared__ __align__(16) unsigned char u4_smem_raw[];
+  Upd4Stage* st = reinterpret_cast<Upd4Stage*>(u4_smem_raw);
+  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
+  const int tid = threadIdx.x, cg = tid & 15, rg = tid >> 4;
+  auto tile_of = [&](int t, int& b, int& row0, int& col0) {
+    const int per_b = tiles_c * tiles_r;
+    b = t / per_b;
+    const int rem = t - b * per_b;
+    row0 = (rem / tiles_c) * kU4Rows;
+    col0 = P.coff + (rem % tiles_c) * kU4Cols;
+  };
+  auto issue = [&](int t, int slot) {
+    int b, row0, col0;
+    tile_of(t, b, row0, col0);
+    Upd4Stage& s = st[slot];
+    const float* __restrict__ Sb = P.src + (long long)b * P.src_bstride;
+    const float* __restrict__ Hb = P.H + (long long)b * n * n;
+    const float* __restrict__ W2b = P.W2 + (long long)b * 32 * P.ncmax;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {  // C: 64 rows x 32 float4
+      const int e = it * 256 + tid, rr = e >> 5, q = e & 31, r = row0 + rr, col = col0 + 4 * q;
+      const bool ok = r < m && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {  // V: 64 rows x 8 float4
+      const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = row0 + rr;
+      const bool ok = r < m && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {  // W2: 32 rows x 32 float4
+      const int e = it * 256 + tid, c = e >> 5, q = e & 31, col = col0 + 4 * q;
+      const bool ok = col < nc;
+      cp_async16(&s.W[c][4 * q], ok ? W2b + (long long)c * P.ncmax + col : W2b, ok);
+    }
+  };
+  int t = blockIdx.x;
+  if (t < ntiles) issue(t, 0);
+  cp_async_commit();
+  for (int it = 0; t < ntiles; t += gridDim.x, ++it) {
+    const int slot = it & 1;
+    const int tn = t + gridDim.x;
+    if (tn < ntiles) issue(tn, slot ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    int b, row0, col0;
+    tile_of(t, b, row0, col0);
+    Upd4Stage& s = st[slot];
+    if (row0 == 0) {
+      // Panel rows 0..31: V is unit lower triangular there.
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int e = q * 256 + tid, rr = e >> 5, c = e & 31;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+    // acc[i][h]: row 4 rg + i, column pair h of this thread's eight (h < 2: 4 cg + 2 h ..;
+    // h >= 2: 64 + 4 cg + 2 (h - 2) ..).
+    float2 acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) acc[i][h] = make_float2(0.f, 0.f);
+#pragma unroll 2
+    for (int c4 = 0; c4 < 32; c4 += 4) {
+      float4 vr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vr[i] = *reinterpret_cast<const float4*>(&s.V[4 * rg + i][c4]);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const float4 xa = *reinterpret_cast<const float4*>(&s.W[c4 + cc][4 * cg]);
+        const float4 xb = *reinterpret_cast<const float4*>(&s.W[c4 + cc][64 + 4 * cg]);
+        const float2 xp[4] = {make_float2(xa.x, xa.y), make_float2(xa.z, xa.w), make_float2(xb.x, xb.y),
+                              make_float2(xb.z, xb.w)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float v = cc == 0 ? vr[i].x : (cc == 1 ? vr[i].y : (cc == 2 ? vr[i].z : vr[i].w));
+          const float2 vv = make_float2(v, v);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) acc[i][h] = __ffma2_rn(vv, xp[h], acc[i][h]);
+        }
+      }
+    }
+    float* __restrict__ Ho = P.H + (long long)b * n * n;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int cl = 64 * hh + 4 * cg, col = col0 + cl;
+      if (col < nc) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = row0 + 4 * rg + i;
+          if (r < m) {
+            const float4 c = *reinterpret_cast<const float4*>(&s.C[4 * rg + i][cl]);
+            *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
+                make_float4(c.x - acc[i][2 * hh].x, c.y - acc[i][2 * hh].y, c.z - acc[i][2 * hh + 1].x,
+                            c.w - acc[i][2 * hh + 1].y);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the slot is refilled by the next iteration's issue
+  }
+  cp_async_wait<0>();
+}
+
 }  // namespace qrb200
