@@ -14,7 +14,7 @@ Arms:
 
 Timing: W warm-up calls per config, then K timed calls, each bracketed by CUDA events on
 the current stream after an L2 flush (a 256 MiB write); ranks barrier before and after.
-``e2e`` repeats the measurement through ``custom_kernel`` with pinned host input and output
+``e2e`` repeats the measurement through ``custom_kernel_host`` with pinned host input and output
 buffers, the host<->device copies inside the timed region.
 """
 
@@ -251,10 +251,9 @@ def run_ours(args, world, rank, local, dist):
             htau = torch.empty(A.shape[:2], dtype=torch.float32).pin_memory()
 
             def e2e_call():
-                dA = hA.to(dev, non_blocking=True)
-                H, tau = custom_kernel(dA)
-                hH.copy_(H, non_blocking=True)
-                htau.copy_(tau, non_blocking=True)
+                # Public host-buffer API: copies in, factorisation, copies out, pipelined in
+                # batch pieces on separate streams and joined into the current stream.
+                api.custom_kernel_host(hA, device=dev, out=(hH, htau))
 
             ts = time_device(e2e_call, args.steps, max(1, args.warmup), flush)
             mine = statistics.mean(ts)

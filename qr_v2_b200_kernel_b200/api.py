@@ -28,7 +28,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["custom_kernel", "geqrf", "workspace_bytes"]
+__all__ = ["custom_kernel", "custom_kernel_host", "geqrf", "workspace_bytes"]
 
 _ws_lock = threading.Lock()
 _ws_cache: dict[tuple[int, int], torch.Tensor] = {}
@@ -93,3 +93,89 @@ def custom_kernel(data: torch.Tensor):
     tau = torch.empty((batch, n), dtype=torch.float32, device=A.device)
     geqrf(A, H, tau)
     return H, tau
+
+
+_chunk_streams: dict[int, list] = {}
+
+
+def _host_chunks(batch: int) -> int:
+    """Pieces a host-buffer call is cut into: enough for copies to overlap the factorisation,
+    few enough that every piece still fills the GPU (at least 32 matrices each)."""
+    return 1 if batch < 64 else min(4, batch // 32)
+
+
+def _streams(device: torch.device, count: int) -> list:
+    with _ws_lock:
+        ss = _chunk_streams.setdefault(device.index, [])
+        while len(ss) < count:
+            ss.append(torch.cuda.Stream(device=device))
+        return ss[:count]
+
+
+def custom_kernel_host(data: torch.Tensor, device=None, out=None, chunks: int | None = None):
+    """Batched QR of a host-resident ``(batch, n, n)`` float32 tensor, results back on the host.
+
+    The batch is cut into up to four contiguous pieces, each on its own CUDA stream of
+    ``device`` (default: the current device): copy in, factor (:func:`custom_kernel`), copy out,
+    so the copies of one piece overlap the factorisation of another (use pinned host memory
+    for that). Every matrix is factored exactly as :func:`custom_kernel` would factor it (a
+    matrix's arithmetic does not depend on its batch), so the results agree bit for bit.
+
+    ``out`` may pass preallocated host tensors ``(H, tau)`` (pinned, ``(batch, n, n)`` and
+    ``(batch, n)``); otherwise pinned ones are allocated. The call returns once the work is
+    enqueued: the results are ready after the device's current stream is synchronised (all
+    pieces are joined back into it).
+    """
+    A = data
+    if not isinstance(A, torch.Tensor):
+        raise TypeError("custom_kernel_host expects a torch.Tensor")
+    if A.dim() != 3 or A.shape[-1] != A.shape[-2]:
+        raise ValueError(f"expected a (batch, n, n) tensor, got shape {tuple(A.shape)}")
+    if A.dtype != torch.float32:
+        raise TypeError(f"expected torch.float32, got {A.dtype}")
+    if A.is_cuda:
+        raise ValueError("custom_kernel_host takes a host tensor; use custom_kernel for device tensors")
+    if not torch.cuda.is_available():
+        raise RuntimeError("qrb200 needs a CUDA device (no CPU fallback)")
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        if dev.type != "cuda":
+            raise ValueError(f"device must be a CUDA device, got {dev}")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+    batch, n = int(A.shape[0]), int(A.shape[-1])
+    if out is None:
+        H_host = torch.empty((batch, n, n), dtype=torch.float32, pin_memory=True)
+        tau_host = torch.empty((batch, n), dtype=torch.float32, pin_memory=True)
+    else:
+        H_host, tau_host = out
+        if tuple(H_host.shape) != (batch, n, n) or tuple(tau_host.shape) != (batch, n):
+            raise ValueError("out tensors have the wrong shape")
+    if batch == 0 or n == 0:
+        return H_host, tau_host
+    A = A.contiguous()
+    k = max(1, min(int(chunks) if chunks else _host_chunks(batch), batch))
+    bounds = [(batch * i // k, batch * (i + 1) // k) for i in range(k)]
+    with torch.cuda.device(dev):
+        if k == 1:  # nothing to overlap: stay on the current stream
+            H, tau = custom_kernel(A.to(dev, non_blocking=True))
+            H_host.copy_(H, non_blocking=True)
+            tau_host.copy_(tau, non_blocking=True)
+            return H_host, tau_host
+        cur = torch.cuda.current_stream(dev)
+        streams = _streams(dev, k)
+        for s in streams:
+            s.wait_stream(cur)
+        for s, (lo, hi) in zip(streams, bounds):
+            with torch.cuda.stream(s):
+                dA = A[lo:hi].to(dev, non_blocking=True)
+                H, tau = custom_kernel(dA)
+                H_host[lo:hi].copy_(H, non_blocking=True)
+                tau_host[lo:hi].copy_(tau, non_blocking=True)
+            # dA, H and tau were allocated on s and are used only there, so the caching
+            # allocator hands their memory to later work on s only.
+        for s in streams:
+            cur.wait_stream(s)
+    return H_host, tau_host

@@ -91,3 +91,20 @@ def test_noalloc_entry_host_checks(lib):
     # beyond the static scratch: rejected before any device call
     assert lib.qrb200_workspace_bytes(2, 4096) > _lib.NOALLOC_SCRATCH_BYTES >= lib.qrb200_workspace_bytes(1, 4096)
     assert f(p, p, p, 2, 4096, 4096 * 4096, None) == _lib.QRB200_ERR_SCRATCH_LIMIT
+
+
+def test_host_api_rejects_bad_inputs_on_cpu():
+    import torch
+
+    from qr_v2_b200_kernel_b200 import custom_kernel_host
+    from qr_v2_b200_kernel_b200.api import _host_chunks
+
+    with pytest.raises(TypeError):
+        custom_kernel_host([[1.0]])
+    with pytest.raises(ValueError):
+        custom_kernel_host(torch.zeros(2, 3, 4))
+    with pytest.raises(TypeError):
+        custom_kernel_host(torch.zeros(2, 3, 3, dtype=torch.float64))
+    # pieces: one below 64 matrices, otherwise at least 32 matrices each, at most four
+    assert _host_chunks(8) == 1 and _host_chunks(63) == 1
+    assert _host_chunks(64) == 2 and _host_chunks(640) == 4
