@@ -28,6 +28,7 @@
 #include "wy_u1.cuh"
 #include "wy_tc.cuh"
 #include "wy_tc128.cuh"
+#include "wy_tc128p.cuh"
 
 namespace qrb200 {
 
@@ -567,6 +568,19 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
 }
 
 
+// Operand ring of the 128-wide GEMM tiles: QRB200_PIPE = 3 (default: three slots, loads one
+// stage ahead, two CTAs per SM), 4 (four slots, two ahead, one CTA per SM) or 0 (the
+// register-staged kernel).
+static int pipe_slots() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_PIPE");
+    v = e ? atoi(e) : 3;
+    if (v != 0 && v != 3 && v != 4) v = 3;
+  }
+  return v;
+}
+
 static cudaError_t tc128_configure() {
   static PerDevice done;
   const int dev = current_device();
@@ -577,6 +591,10 @@ static cudaError_t tc128_configure() {
   if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_Y>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_UPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<4>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<4>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   done.mark(dev);
   return cudaSuccess;
 }
@@ -837,7 +855,14 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   }
   {
     LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
-    tc_gemm128_kernel<MODE_UPD><<<dim3(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, s>>>(gp);
+    const dim3 grid(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch);
+    const int ps = pipe_slots();
+    if (ps == 4 && nsw == 1)
+      tc_gemm128_pipe_kernel<MODE_UPD, 4><<<grid, 128, pipe128_smem<4>(), s>>>(gp);
+    else if (ps == 3 && nsw == 1)
+      tc_gemm128_pipe_kernel<MODE_UPD, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
+    else
+      tc_gemm128_kernel<MODE_UPD><<<grid, 128, kGemm128Smem, s>>>(gp);
   }
   return cudaGetLastError();
 }
@@ -911,7 +936,14 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
     gp.w = ow;
     {
       LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
-      tc_gemm128_kernel<MODE_Y><<<dim3(1, cdiv(m, 128), (unsigned)batch), 128, kGemm128Smem, sp>>>(gp);
+      const dim3 grid(1, cdiv(m, 128), (unsigned)batch);
+      const int ps = pipe_slots();
+      if (ps == 4)
+        tc_gemm128_pipe_kernel<MODE_Y, 4><<<grid, 128, pipe128_smem<4>(), sp>>>(gp);
+      else if (ps == 3)
+        tc_gemm128_pipe_kernel<MODE_Y, 3><<<grid, 128, pipe128_smem<3>(), sp>>>(gp);
+      else
+        tc_gemm128_kernel<MODE_Y><<<grid, 128, kGemm128Smem, sp>>>(gp);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const int split_at = k0 + 2 * kOB;  // U1 = columns [k0 + ow, split_at), U2 = [split_at, n)

@@ -116,10 +116,21 @@ __global__ void __launch_bounds__(128) tc_vtcw_kernel(WyParams P) {
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
+  // C rows kPrefetchAhead chunks ahead are requested into L2 (one 128-byte line per thread).
+  constexpr int kPrefetchAhead = 4;
+  auto prefetch_chunk = [&](int ch) {
+    if (GRAM || ch >= nchunks || tid >= kWChunk * 5) return;
+    const int rr = tid / 5, q = tid % 5, r = r_begin + ch * kWChunk + rr;
+    const int cl = min(32 * q, nc - col0 - 1);
+    if (r < r_end && cl >= 0) prefetch_l2(Sb + (long long)(k + r) * n + k + w + col0 + cl);
+  };
+#pragma unroll
+  for (int c = 1; c <= kPrefetchAhead; ++c) prefetch_chunk(c);
   if (nchunks > 0) load(0);
   for (int ch = 0; ch < nchunks; ++ch) {
     const int s = ch & 1;
     VtcwStage<W>& st = sh.st[s];
+    prefetch_chunk(ch + 1 + kPrefetchAhead);
     if (ch >= 2) ok = mbar_wait(&sh.mbar[s], ((ch >> 1) - 1) & 1) && ok;
 #pragma unroll
     for (int it = 0; it < NV; ++it) {

@@ -1,0 +1,200 @@
+// 128 x 128 x 128 3xTF32 tcgen05 tile (Y = V T^T, or C -= Y W) with its operands streamed by
+// cp.async: each 16-byte piece of raw fp32 lands directly at its place in the K-major
+// core-matrix layout of the MMA operand (the hi buffer of a four-slot ring), two K stages ahead
+// of the MMAs. The thread that requested a piece splits it in place once it has arrived
+// (hi = tf32_rna(x) over x, lo = x - hi beside it), so no operand passes through registers while
+// its load is in flight and the load latency is covered by two stages of tensor-core work.
+// Same tiles, same arithmetic as tc_gemm128_kernel (wy_tc128.cuh), so results agree bit for bit.
+// MODE_UPD takes the W^T of a single row split (nsplit == 1).
+#pragma once
+
+#include "wy_simt2.cuh"
+#include "wy_tc128.cuh"
+
+namespace qrb200 {
+
+// SLOTS K stages of 16 resident; loads run SLOTS - 2 stages ahead (a slot is refilled once the
+// MMAs of the stage two before the current one are done). Four slots: one CTA per SM; three:
+// two CTAs per SM.
+template <int SLOTS>
+struct Pipe128Shared {
+  Gemm128Stage st[SLOTS];
+  uint64_t mbar[SLOTS];
+  uint32_t tmem;
+};
+template <int SLOTS>
+constexpr size_t pipe128_smem() { return sizeof(Pipe128Shared<SLOTS>) + 1024; }
+
+template <int MODE, int SLOTS>
+__global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
+  constexpr int kPipeSlots = SLOTS, kAhead = SLOTS - 2;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  Pipe128Shared<SLOTS>& sh = *reinterpret_cast<Pipe128Shared<SLOTS>*>(align1024(smem_raw));
+  constexpr uint32_t RS = (kGChunk / 4) * 128, CS = 128;
+  constexpr int NK = kOB / kGChunk;  // 8 K stages
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bidx = blockIdx.z;
+  const int n = P.n, k = P.k, w = P.w, m = n - k;
+  const int ncols = (MODE == MODE_Y) ? kOB : P.cend - k - w;
+  const int col0 = (MODE == MODE_UPD ? P.coff : 0) + blockIdx.x * 128, row0 = blockIdx.y * 128;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
+  const float* __restrict__ Bsrc = (MODE == MODE_Y) ? P.T + (long long)bidx * kOB * kOB
+                                                    : P.Wp + (long long)bidx * P.ncmax * kOB;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kPipeSlots; ++s) mbar_init(&sh.mbar[s], 1);
+    fence_async_smem();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+  constexpr uint32_t idesc = make_idesc_tf32(128, 128, false, false);
+  bool ok = true;
+  if (MODE == MODE_UPD && row0 + tid < m) {
+    // The epilogue's slice of C (this thread's row, 128 columns) starts moving HBM -> L2 now,
+    // under the K loop, instead of after it.
+    const float* crow = P.src + (long long)bidx * P.src_bstride + (long long)(k + row0 + tid) * n + k + w + col0;
+    const int last = min(ncols - col0, 128) - 1;
+    if (last >= 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (32 * q <= last) prefetch_l2(crow + 32 * q);
+      prefetch_l2(crow + last);
+    }
+  }
+
+  // Piece it of this thread: row rr of the tile, column quad cq of the K slice (8 lanes fill
+  // one 128-byte core matrix) -- the mapping of tc_gemm128_kernel.
+  auto coord = [&](int it, int& rr, int& cq) {
+    const int idx = it * 128 + tid;
+    rr = (idx & 7) + 8 * (idx >> 5);
+    cq = (idx >> 3) & 3;
+  };
+  auto issue = [&](int kc) {
+    Gemm128Stage& st = sh.st[kc % kPipeSlots];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      int rr, cq;
+      coord(it, rr, cq);
+      const int c = kc * kGChunk + 4 * cq;
+      const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
+      const int r = row0 + rr;
+      const bool va = r < m && c < w;
+      const float* sa = (MODE == MODE_Y) ? Hb + (long long)(k + r) * n + k + c : Yb + (long long)r * kOB + c;
+      cp_async16(st.a_hi + off, va ? sa : Hb, va);
+      const int j = col0 + rr;
+      const bool vb = j < ncols && c < w;
+      cp_async16(st.b_hi + off, vb ? Bsrc + (long long)j * kOB + c : Bsrc, vb);
+    }
+  };
+  auto split_inplace = [](float* hi, float* lo, uint32_t off) {
+    const float4 x = *reinterpret_cast<const float4*>(hi + off);
+    float4 h, l;
+    split4(x, h, l);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+  };
+
+#pragma unroll
+  for (int s = 0; s < kAhead; ++s) {
+    issue(s);
+    cp_async_commit();
+  }
+  for (int kc = 0; kc < NK; ++kc) {
+    // Refill: stage kc + kAhead goes into the slot of stage kc - 2, once its MMAs are done.
+    if (kc + kAhead < NK) {
+      if (kc >= 2) ok = mbar_wait(&sh.mbar[(kc - 2) % kPipeSlots], (uint32_t)(((kc - 2) / kPipeSlots) & 1)) && ok;
+      issue(kc + kAhead);
+    }
+    cp_async_commit();
+    cp_async_wait<kAhead>();  // this thread's pieces of stage kc have landed
+    Gemm128Stage& st = sh.st[kc % kPipeSlots];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      int rr, cq;
+      coord(it, rr, cq);
+      const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
+      if (MODE == MODE_Y && row0 == 0) {
+        // V is unit lower trapezoidal: rows <= column hold R in H.
+        const int r = rr, c = kc * kGChunk + 4 * cq;
+        float4 x = *reinterpret_cast<const float4*>(st.a_hi + off);
+        x.x = (r > c) ? x.x : (r == c ? 1.f : 0.f);
+        x.y = (r > c + 1) ? x.y : (r == c + 1 ? 1.f : 0.f);
+        x.z = (r > c + 2) ? x.z : (r == c + 2 ? 1.f : 0.f);
+        x.w = (r > c + 3) ? x.w : (r == c + 3 ? 1.f : 0.f);
+        if (c >= w) x = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(st.a_hi + off) = x;
+      }
+      split_inplace(st.a_hi, st.a_lo, off);
+      split_inplace(st.b_hi, st.b_lo, off);
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ah = smem_u32(st.a_hi), al = smem_u32(st.a_lo);
+      const uint32_t bh = smem_u32(st.b_hi), bl = smem_u32(st.b_lo);
+#pragma unroll
+      for (int ks = 0; ks < kGChunk / 8; ++ks)
+        mma_tf32x3(tmem, make_sdesc(ah + ks * 2 * CS, CS, RS), make_sdesc(al + ks * 2 * CS, CS, RS),
+                   make_sdesc(bh + ks * 2 * CS, CS, RS), make_sdesc(bl + ks * 2 * CS, CS, RS), idesc,
+                   kc > 0 || ks > 0);
+      mma_commit(&sh.mbar[kc % kPipeSlots]);
+    }
+  }
+  cp_async_wait<0>();
+  // Epilogue (as tc_gemm128_kernel): thread t owns tile row t; the C slice for the next 32
+  // columns is requested before the current one is processed.
+  const int r = row0 + tid;
+  const bool row_ok = r < m;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
+  const long long roff = (long long)(k + r) * n + k + w;
+  float4 cv[8];
+  auto load_c = [&](int q) {
+    const int cbase = col0 + q * 32;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      cv[e] = (MODE == MODE_UPD && row_ok && cbase + 4 * e < ncols)
+                  ? *reinterpret_cast<const float4*>(Sb + roff + cbase + 4 * e)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  if (MODE == MODE_UPD) load_c(0);
+  {
+    const int last = NK - 1;
+    ok = mbar_wait(&sh.mbar[last % kPipeSlots], (uint32_t)((last / kPipeSlots) & 1)) && ok;
+  }
+  tc_fence_after();
+#pragma unroll 1
+  for (int q = 0; q < 4; ++q) {
+    float pv[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, pv);
+    float4 cur[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cur[e] = cv[e];
+    if (MODE == MODE_UPD && q + 1 < 4) load_c(q + 1);
+    if (!ok || !row_ok) continue;
+    const int cbase = col0 + q * 32;
+    if (MODE == MODE_Y) {
+      float* yrow = P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + cbase;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(yrow + e) = make_float4(pv[e], pv[e + 1], pv[e + 2], pv[e + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (cbase + 4 * e < ncols)
+          *reinterpret_cast<float4*>(Ho + roff + cbase + 4 * e) =
+              make_float4(cur[e].x - pv[4 * e], cur[e].y - pv[4 * e + 1], cur[e].z - pv[4 * e + 2], cur[e].w - pv[4 * e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+}  // namespace qrb200
