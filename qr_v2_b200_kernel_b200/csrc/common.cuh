@@ -65,4 +65,24 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float xnorm2) {
   return r;
 }
 
+// Reflector scalars as make_reflector, with the square root and the reciprocal from the
+// hardware approximations, the reciprocal square root refined by one Newton step
+// (y <- y (3 - x y^2) / 2): about 1 ulp. Norms outside [1e-30, 1e30] take the correctly
+// rounded path, where the approximations lose range.
+__device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnorm2) {
+  const float nrm2 = fmaf(alpha, alpha, xnorm2);
+  if (!(nrm2 > 1e-30f && nrm2 < 1e30f)) return make_reflector(alpha, xnorm2);
+  float y = rsqrtf(nrm2);
+  y = y * fmaf(-0.5f * nrm2, y * y, 1.5f);
+  const float nrm = nrm2 * y;
+  const float aa = fabsf(alpha);
+  const float inv = __fdividef(1.f, aa + nrm);
+  Reflector r;
+  const bool need = xnorm2 > 0.f;
+  r.diag = need ? (alpha >= 0.f ? -nrm : nrm) : alpha;
+  r.tau = need ? fmaf(aa, y, 1.f) : 0.f;
+  r.scale = need ? (alpha >= 0.f ? inv : -inv) : 0.f;
+  return r;
+}
+
 }  // namespace qrb200

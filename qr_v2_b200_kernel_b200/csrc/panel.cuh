@@ -278,13 +278,15 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
         for (int q = 1; q < CPW; ++q) t = (q == oq) ? a[q][i] : t;
         x[i] = t;
       }
-      float s = 0.f;
+      // Four independent partial sums shorten the dependent FMA chain.
+      float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) s = (lane + 32 * i > j) ? fmaf(x[i], x[i], s) : s;
+      for (int i = 0; i < RPL; ++i) sp[i & 3] = (lane + 32 * i > j) ? fmaf(x[i], x[i], sp[i & 3]) : sp[i & 3];
+      float s = (sp[0] + sp[1]) + (sp[2] + sp[3]);
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
       const float alpha = __shfl_sync(kFullMask, x[0], j);
-      const Reflector rf = make_reflector(alpha, s);
+      const Reflector rf = make_reflector_fast(alpha, s);
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
         const int lr = lane + 32 * i;
@@ -308,10 +310,13 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
     float dq[CPW];
 #pragma unroll
     for (int q = 0; q < CPW; ++q) {
-      float d = 0.f;
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) d = fmaf(v[i], a[q][i], d);
-      dq[q] = d;
+      for (int i = 0; i < RPL; i += 2) {
+        d0 = fmaf(v[i], a[q][i], d0);
+        if (i + 1 < RPL) d1 = fmaf(v[i + 1], a[q][i + 1], d1);
+      }
+      dq[q] = d0 + d1;
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1)

@@ -415,6 +415,17 @@ static bool panel_fw() {
   return v == 1;
 }
 
+// Smallest matrix order whose panels of up to 512 rows use the factor-warp kernel
+// (QRB200_FW_MIN_N; the owner kernel below it).
+static int fw_min_n() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_FW_MIN_N");
+    v = e ? atoi(e) : 513;
+  }
+  return v;
+}
+
 static bool panel_lookahead() {
   static int v = -1;
   if (v < 0) {
@@ -445,7 +456,7 @@ static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batc
     if (clr == 512) return launch_cl<16, false>(q, cdiv(m, 512), batch, s);
     return launch_cl<8, false>(q, cdiv(m, 256), batch, s);
   }
-  if (panel_fw() && pp.n > 512) {
+  if (panel_fw() && pp.n >= fw_min_n()) {
     if (m <= 128) return launch_fw<4>(q, batch, s);
     if (m <= 256) return launch_fw<8>(q, batch, s);
     if (m <= 512) return launch_fw<16>(q, batch, s);
