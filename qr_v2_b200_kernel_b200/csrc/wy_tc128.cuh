@@ -208,8 +208,9 @@ struct TbuildParams {
   float* Tout;            // batch x 128 x 128
   int ow;                 // outer block width (multiple of 32, <= 128)
 };
+// T's strictly lower part is zero, so it holds the Gram blocks the recurrence reads instead:
+// G[i][j] (block(i) < block(j)) lives at T[j][i]. 79 KB: two CTAs per SM.
 struct TbuildShared {
-  float G[kOB][kOB + 1];
   float T[kOB][kOB + 1];
   float X[96][33];
 };
@@ -236,11 +237,12 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
       const int e = 4 * (t * 256 + tid), i = e / kOB, j = e % kOB;
-      sh.G[i][j] = g[t].x; sh.G[i][j + 1] = g[t].y; sh.G[i][j + 2] = g[t].z; sh.G[i][j + 3] = g[t].w;
-      sh.T[i][j] = 0.f; sh.T[i][j + 1] = 0.f; sh.T[i][j + 2] = 0.f; sh.T[i][j + 3] = 0.f;
+      if ((i >> 5) < (j >> 5)) {  // cross-panel Gram block, stored transposed below the diagonal
+        sh.T[j][i] = g[t].x; sh.T[j + 1][i] = g[t].y; sh.T[j + 2][i] = g[t].z; sh.T[j + 3][i] = g[t].w;
+      }
     }
   }
-  __syncthreads();  // the zero fill must land before the diagonal blocks are written
+  __syncthreads();
   for (int e = tid; e < 4 * 32 * 32; e += 256) {
     const int blk = e / 1024, i = (e / 32) % 32, j = e % 32;
     if (32 * blk < ow) sh.T[32 * blk + i][32 * blk + j] = P.Tin[(long long)b * 4096 + e];
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
         const float t = sh.T[r + c][r + tj];
 #pragma unroll
         for (int q = 0; q < 12; ++q)
-          if (q < nq) acc[q] = fmaf(sh.G[ti + 8 * q][r + c], t, acc[q]);
+          if (q < nq) acc[q] = fmaf(sh.T[r + c][ti + 8 * q], t, acc[q]);  // G[ti + 8q][r + c]
       }
 #pragma unroll
       for (int q = 0; q < 12; ++q)
@@ -288,7 +290,12 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
     }
     __syncthreads();
   }
-  for (int e = tid; e < kOB * kOB; e += 256) P.Tout[(long long)b * kOB * kOB + e] = sh.T[e / kOB][e % kOB];
+  // Upper triangle of the first ow columns; the Gram storage below the diagonal and any block
+  // column the recurrence did not reach are zero in T.
+  for (int e = tid; e < kOB * kOB; e += 256) {
+    const int i = e / kOB, j = e % kOB;
+    P.Tout[(long long)b * kOB * kOB + e] = (i > j || j >= ow) ? 0.f : sh.T[i][j];
+  }
 }
 
 // ---------------------------------------------------------------------------------------
