@@ -599,6 +599,10 @@ static cudaError_t tc128_configure() {
   cudaError_t e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, false, 3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, true, 3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, false, 4>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, true, 4>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_Y>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_UPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
@@ -862,7 +866,12 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   gp.coff = coff;
   {
     LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
-    tc_vtcw_kernel<kOB, false><<<dim3(cdiv(nc, kTcCols), nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), s>>>(wp);
+    const dim3 grid(cdiv(nc, kTcCols), nsw, (unsigned)batch);
+    switch (pipe_slots()) {
+      case 3: tc_vtcw_pipe_kernel<kOB, false, 3><<<grid, 128, vtcw_pipe_smem<kOB, false, 3>(), s>>>(wp); break;
+      case 4: tc_vtcw_pipe_kernel<kOB, false, 4><<<grid, 128, vtcw_pipe_smem<kOB, false, 4>(), s>>>(wp); break;
+      default: tc_vtcw_kernel<kOB, false><<<grid, 128, vtcw_smem<kOB>(), s>>>(wp);
+    }
   }
   {
     LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
@@ -930,7 +939,12 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
     g.ncmax = kOB;
     {
       LaunchScope ls(K_GRAM, 2.0 * bm * ow * ow, 4.0 * bm * ow);
-      tc_vtcw_kernel<kOB, true><<<dim3(1, nsw, (unsigned)batch), 128, vtcw_smem<kOB>(), sp>>>(g);
+      const dim3 grid(1, nsw, (unsigned)batch);
+      switch (pipe_slots()) {
+        case 3: tc_vtcw_pipe_kernel<kOB, true, 3><<<grid, 128, vtcw_pipe_smem<kOB, true, 3>(), sp>>>(g); break;
+        case 4: tc_vtcw_pipe_kernel<kOB, true, 4><<<grid, 128, vtcw_pipe_smem<kOB, true, 4>(), sp>>>(g); break;
+        default: tc_vtcw_kernel<kOB, true><<<grid, 128, vtcw_smem<kOB>(), sp>>>(g);
+      }
     }
     {
       TbuildParams tp{ws.Gp, nsw, ws.T, ws.Tob, ow};

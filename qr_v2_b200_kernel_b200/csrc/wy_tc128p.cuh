@@ -197,4 +197,169 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
+// ---------------------------------------------------------------------------------------
+// W^T = C^T V (or the Gram G = V^T V) over one row split, as tc_vtcw_kernel (wy_tc128.cuh),
+// with the rows streamed by cp.async straight into the SW128_32B operand layout and split in
+// place (V masked to its unit lower trapezoid in the panel's first 128 rows). Same tiles and
+// arithmetic, so results agree bit for bit.
+template <int W, bool GRAM, int SLOTS>
+struct VtcwPipeShared {
+  VtcwStage<W> st[SLOTS];
+  uint64_t mbar[SLOTS];
+  uint32_t tmem;
+};
+template <int W, bool GRAM, int SLOTS>
+constexpr size_t vtcw_pipe_smem() { return sizeof(VtcwPipeShared<W, GRAM, SLOTS>) + 1024; }
+
+template <int W, bool GRAM, int SLOTS>
+__global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
+  constexpr int kAhead = SLOTS - 2;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  VtcwPipeShared<W, GRAM, SLOTS>& sh = *reinterpret_cast<VtcwPipeShared<W, GRAM, SLOTS>*>(align1024(smem_raw));
+  constexpr uint32_t LBO = 512, SBO_C = (kTcCols / 32) * 512, SBO_V = (W / 32) * 512;
+  constexpr int NV = W / 32;
+  constexpr int NC = GRAM ? 0 : 4;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, m = n - k;
+  const int nc = GRAM ? w : P.cend - k - w;
+  const int col0 = (GRAM ? 0 : P.coff) + blockIdx.x * kTcCols;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(m, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kWChunk - 1) / kWChunk : 0;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < SLOTS; ++s) mbar_init(&sh.mbar[s], 1);
+    fence_async_smem();
+  }
+  if (warp == 0) tmem_alloc(&sh.tmem, W);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem;
+  constexpr uint32_t idesc = make_idesc_tf32(128, W, true, true);
+  bool ok = true;
+  const int q8 = lane & 7, kr = lane >> 3;
+  auto v_coord = [&](int it, int& c, int& kk) {
+    const int atom = it * 4 + warp;
+    c = (atom % NV) * 32 + 4 * q8;
+    kk = (atom / NV) * 4 + kr;
+  };
+  auto c_coord = [&](int it, int& mn, int& kk) {
+    const int atom = it * 4 + warp;
+    mn = (atom & 3) * 32 + 4 * q8;
+    kk = (atom >> 2) * 4 + kr;
+  };
+  auto issue = [&](int ch) {
+    VtcwStage<W>& st = sh.st[ch % SLOTS];
+    const int r0 = r_begin + ch * kWChunk;
+#pragma unroll
+    for (int it = 0; it < NV; ++it) {
+      int c, kk;
+      v_coord(it, c, kk);
+      const int r = r0 + kk;
+      const bool ok_v = r < r_end && c < w;
+      cp_async16(st.v_hi + (sw32_off(c, kk, LBO, SBO_V) >> 2), ok_v ? Hb + (long long)(k + r) * n + k + c : Hb, ok_v);
+    }
+#pragma unroll
+    for (int it = 0; it < NC; ++it) {
+      int mn, kk;
+      c_coord(it, mn, kk);
+      const int r = r0 + kk, col = col0 + mn;
+      const bool ok_c = r < r_end && col < nc;
+      cp_async16(st.c_hi + (sw32_off(mn, kk, LBO, SBO_C) >> 2),
+                 ok_c ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok_c);
+    }
+  };
+  auto split_inplace = [](float* hi, float* lo, uint32_t off) {
+    const float4 x = *reinterpret_cast<const float4*>(hi + off);
+    float4 h, l;
+    split4(x, h, l);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+  };
+
+#pragma unroll
+  for (int s = 0; s < kAhead; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit();
+  }
+  for (int ch = 0; ch < nchunks; ++ch) {
+    if (ch + kAhead < nchunks) {
+      if (ch >= 2) ok = mbar_wait(&sh.mbar[(ch - 2) % SLOTS], (uint32_t)(((ch - 2) / SLOTS) & 1)) && ok;
+      issue(ch + kAhead);
+    }
+    cp_async_commit();
+    cp_async_wait<kAhead>();
+    VtcwStage<W>& st = sh.st[ch % SLOTS];
+    const int r0 = r_begin + ch * kWChunk;
+#pragma unroll
+    for (int it = 0; it < NV; ++it) {
+      int c, kk;
+      v_coord(it, c, kk);
+      const uint32_t off = sw32_off(c, kk, LBO, SBO_V) >> 2;
+      const int r = r0 + kk;
+      if (r < c + 4) {  // unit lower trapezoid: R sits on and above the diagonal in H
+        float4 x = *reinterpret_cast<const float4*>(st.v_hi + off);
+        x.x = (c >= w) ? 0.f : ((r > c) ? x.x : (r == c ? 1.f : 0.f));
+        x.y = (c + 1 >= w) ? 0.f : ((r > c + 1) ? x.y : (r == c + 1 ? 1.f : 0.f));
+        x.z = (c + 2 >= w) ? 0.f : ((r > c + 2) ? x.z : (r == c + 2 ? 1.f : 0.f));
+        x.w = (c + 3 >= w) ? 0.f : ((r > c + 3) ? x.w : (r == c + 3 ? 1.f : 0.f));
+        if (r >= r_end) x = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(st.v_hi + off) = x;
+      }
+      split_inplace(st.v_hi, st.v_lo, off);
+    }
+#pragma unroll
+    for (int it = 0; it < NC; ++it) {
+      int mn, kk;
+      c_coord(it, mn, kk);
+      split_inplace(st.c_hi, st.c_lo, sw32_off(mn, kk, LBO, SBO_C) >> 2);
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ach = smem_u32(GRAM ? st.v_hi : st.c_hi), acl = smem_u32(GRAM ? st.v_lo : st.c_lo);
+      const uint32_t sbo_a = GRAM ? SBO_V : SBO_C;
+      const uint32_t bvh = smem_u32(st.v_hi), bvl = smem_u32(st.v_lo);
+#pragma unroll
+      for (int ks = 0; ks < kWChunk / 8; ++ks) {
+        mma_tf32x3(tmem, make_sdesc_sw32(ach + ks * 2 * sbo_a, LBO, sbo_a), make_sdesc_sw32(acl + ks * 2 * sbo_a, LBO, sbo_a),
+                   make_sdesc_sw32(bvh + ks * 2 * SBO_V, LBO, SBO_V), make_sdesc_sw32(bvl + ks * 2 * SBO_V, LBO, SBO_V),
+                   idesc, ch > 0 || ks > 0);
+      }
+      mma_commit(&sh.mbar[ch % SLOTS]);
+    }
+  }
+  cp_async_wait<0>();
+  if (nchunks > 0) {
+    const int last = nchunks - 1;
+    ok = mbar_wait(&sh.mbar[last % SLOTS], (uint32_t)((last / SLOTS) & 1)) && ok;
+  }
+  tc_fence_after();
+  const int col = col0 + tid;
+  float* out = P.Wp + (((long long)bidx * P.nsplit + split) * P.ncmax + col) * W;
+#pragma unroll 1
+  for (int q = 0; q < W / 32; ++q) {
+    float wv[32];
+    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, wv);
+    if (nchunks == 0 || !ok) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) wv[i] = 0.f;
+    }
+    if (col < (GRAM ? W : nc)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(out + q * 32 + i) = make_float4(wv[i], wv[i + 1], wv[i + 2], wv[i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, W);
+}
+
 }  // namespace qrb200
