@@ -109,20 +109,26 @@ struct PanelShared {
   float T[32][33];         // T factor (CTA 0)
 };
 
-// LARFT T from G[c][j] = v_c . v_j (c < j) and tau, by one warp (lane = row of T):
-// T[i][j] = -tau_j sum_{i <= c < j} T[i][c] G[c][j], T[j][j] = tau_j (submission.py:129-137).
-__device__ __forceinline__ void larft_from_gram(float (&T)[32][33], const float (&G)[32][33], const float* tau,
-                                                int jmax) {
-  const int lane = threadIdx.x & 31;
-  for (int j = 0; j < jmax; ++j) {
-    float acc = 0.f;
-    for (int c = 0; c < j; ++c) {
-      const float t = T[lane][c];
-      acc = (c >= lane) ? fmaf(t, G[c][j], acc) : acc;
+// T of a 32-column panel by one warp from the Gram entries G[c][i] = v_c . v_i (c < i) and
+// tau: T^-1 = diag(1/tau) + striu(V^T V) (the compact-WY factor of H_0 .. H_{k-1}, cf. the LARFT
+// recurrence of submission.py:129-137, which builds the same T column by column). Lane j solves
+// U t = e_j by column-oriented back substitution, t_i = tau_i (e_j - sum_{c>i} U_ic t_c)_i, so
+// no reciprocal is formed and tau_i = 0 (an identity reflector) gives a zero row and column.
+__device__ __forceinline__ void larft_inverse_warp(float (&T)[32][33], const float (&G)[32][33], const float* tau,
+                                                   int jmax) {
+  const int j = threadIdx.x & 31;
+  float r[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) r[i] = (i == j) ? 1.f : 0.f;
+#pragma unroll
+  for (int i = 31; i >= 0; --i) {
+    float ti = 0.f;
+    if (i < jmax) {
+      ti = (i <= j) ? r[i] * tau[i] : 0.f;
+#pragma unroll
+      for (int c = 0; c < i; ++c) r[c] = fmaf(-G[c][i], ti, r[c]);
     }
-    const float tj = tau[j];
-    T[lane][j] = (lane < j) ? -tj * acc : (lane == j ? tj : 0.f);
-    __syncwarp();
+    T[i][j] = ti;
   }
 }
 
@@ -240,7 +246,7 @@ __device__ __forceinline__ void factor_panel_cols(float (&a)[RPL], const int w, 
   }
   if (HAS_T && p == 0) {
     __syncthreads();
-    if (c == 0) larft_from_gram(sh.T, sh.G, sh.tau, jmax);
+    if (c == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
   }
 }
 
@@ -336,7 +342,7 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
   }
   if (HAS_T) {
     __syncthreads();
-    if (g == 0) larft_from_gram(sh.T, sh.G, sh.tau, jmax);
+    if (g == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
   }
 }
 

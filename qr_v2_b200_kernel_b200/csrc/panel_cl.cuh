@@ -96,29 +96,6 @@ __device__ __forceinline__ bool cl_wait(uint64_t* mbar, uint32_t parity) {
   return false;
 }
 
-// T of a 32-column panel by one warp from the Gram entries G[c][i] = v_c . v_i (c < i) and
-// tau: T^-1 = diag(1/tau) + striu(V^T V) (the compact-WY factor of H_0 .. H_{k-1}, cf. the LARFT
-// recurrence of submission.py:129-137, which builds the same T column by column). Lane j solves
-// U t = e_j by column-oriented back substitution, t_i = tau_i (e_j - sum_{c>i} U_ic t_c)_i, so
-// no reciprocal is formed and tau_i = 0 (an identity reflector) gives a zero row and column.
-__device__ __forceinline__ void larft_inverse_warp(float (&T)[32][33], const float (&G)[32][33], const float* tau,
-                                                   int jmax) {
-  const int j = threadIdx.x & 31;
-  float r[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) r[i] = (i == j) ? 1.f : 0.f;
-#pragma unroll
-  for (int i = 31; i >= 0; --i) {
-    float ti = 0.f;
-    if (i < jmax) {
-      ti = (i <= j) ? r[i] * tau[i] : 0.f;
-#pragma unroll
-      for (int c = 0; c < i; ++c) r[c] = fmaf(-G[c][i], ti, r[c]);
-    }
-    T[i][j] = ti;
-  }
-}
-
 __device__ __forceinline__ void cl_barrier_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }

@@ -134,7 +134,7 @@ __device__ __forceinline__ void factor_panel_la(float (&a)[CPW][RPL], const int 
     }
   }
   __syncthreads();
-  if (g == 0) larft_from_gram(sh.T, sh.G, sh.tau, jmax);
+  if (g == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
 }
 
 // One CTA per panel (m <= 32 * RPL rows), coalesced staged load and store as in
