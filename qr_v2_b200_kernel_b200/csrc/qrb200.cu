@@ -145,7 +145,7 @@ static bool use_single_la(int n) {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("QRB200_SINGLE_MIN_N");
-    v = e ? atoi(e) : 1024;
+    v = e ? atoi(e) : 1025;
   }
   return n >= v;
 }
@@ -877,9 +877,9 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
     LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
     const dim3 grid(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch);
     const int ps = pipe_slots();
-    if (ps == 4 && nsw == 1)
+    if (ps == 4 && nsw <= 2)
       tc_gemm128_pipe_kernel<MODE_UPD, 4><<<grid, 128, pipe128_smem<4>(), s>>>(gp);
-    else if (ps == 3 && nsw == 1)
+    else if (ps == 3 && nsw <= 2)
       tc_gemm128_pipe_kernel<MODE_UPD, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
     else
       tc_gemm128_kernel<MODE_UPD><<<grid, 128, kGemm128Smem, s>>>(gp);

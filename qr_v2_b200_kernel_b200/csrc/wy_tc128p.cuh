@@ -5,7 +5,7 @@
 // (hi = tf32_rna(x) over x, lo = x - hi beside it), so no operand passes through registers while
 // its load is in flight and the load latency is covered by two stages of tensor-core work.
 // Same tiles, same arithmetic as tc_gemm128_kernel (wy_tc128.cuh), so results agree bit for bit.
-// MODE_UPD takes the W^T of a single row split (nsplit == 1).
+// MODE_UPD takes W^T as one or two row-split partials (nsplit <= 2).
 #pragma once
 
 #include "wy_simt2.cuh"
@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
   const float* __restrict__ Bsrc = (MODE == MODE_Y) ? P.T + (long long)bidx * kOB * kOB
-                                                    : P.Wp + (long long)bidx * P.ncmax * kOB;
+                                                    : P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB;
 
   if (tid == 0) {
 #pragma unroll
@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
       const int j = col0 + rr;
       const bool vb = j < ncols && c < w;
       cp_async16(st.b_hi + off, vb ? Bsrc + (long long)j * kOB + c : Bsrc, vb);
+      if (MODE == MODE_UPD && P.nsplit == 2)  // second row-split partial, parked in b_lo
+        cp_async16(st.b_lo + off, vb ? Bsrc + (long long)P.ncmax * kOB + (long long)j * kOB + c : Bsrc, vb);
     }
   };
   auto split_inplace = [](float* hi, float* lo, uint32_t off) {
@@ -130,7 +132,19 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
         *reinterpret_cast<float4*>(st.a_hi + off) = x;
       }
       split_inplace(st.a_hi, st.a_lo, off);
-      split_inplace(st.b_hi, st.b_lo, off);
+      if (MODE == MODE_UPD && P.nsplit == 2) {  // W = partial 0 + partial 1, then split
+        const float4 x0 = *reinterpret_cast<const float4*>(st.b_hi + off);
+        const float4 x1 = *reinterpret_cast<const float4*>(st.b_lo + off);
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        x.x += x0.x; x.y += x0.y; x.z += x0.z; x.w += x0.w;
+        x.x += x1.x; x.y += x1.y; x.z += x1.z; x.w += x1.w;
+        float4 h, l;
+        split4(x, h, l);
+        *reinterpret_cast<float4*>(st.b_hi + off) = h;
+        *reinterpret_cast<float4*>(st.b_lo + off) = l;
+      } else {
+        split_inplace(st.b_hi, st.b_lo, off);
+      }
     }
     fence_async_smem();
     __syncthreads();
