@@ -634,6 +634,18 @@ static bool wy3_enabled() {
   return v == 1;
 }
 
+// Narrow updates of the two-level schedule through the one-launch clustered kernel for
+// matrices of order >= QRB200_NARROW_U1_MIN_N (default 1024: it helps at small batch and
+// tall panels, and loses to the streaming kernels at n = 512 and batch 640).
+static bool narrow_u1(int n) {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_NARROW_U1_MIN_N");
+    v = e ? atoi(e) : 1024;
+  }
+  return n >= v;
+}
+
 // Widest update (columns) taken by the one-launch clustered kernel (QRB200_U1_MAX, 0 = off).
 static int u1_max_cols() {
   static int v = -1;
@@ -913,7 +925,7 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
       }
       if (e != cudaSuccess) return e;
       if (kb + w < k0 + ow) {
-        e = launch_wy(src, sbs, H, Tslot, 4 * kNB * kNB, ws, batch, n, kb, w, 0, k0 + ow, sp);
+        e = launch_wy(src, sbs, H, Tslot, 4 * kNB * kNB, ws, batch, n, kb, w, 0, k0 + ow, sp, narrow_u1(n));
         if (e != cudaSuccess) return e;
       }
     }
