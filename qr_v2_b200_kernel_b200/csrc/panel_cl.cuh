@@ -41,10 +41,13 @@ constexpr int kClWarps = 8;
 constexpr int kClThreads = 32 * kClWarps;
 constexpr int kClMaxCta = 16;
 constexpr int kDevStatusClusterTimeout = 7;
+// Row stride of the partial-dot slots: 36 floats put the 16 source rows on different banks, so
+// the lane-parallel totals read them without conflicts (a 32-float stride put them all on one).
+constexpr int kClSlotLd = 36;
 
 template <int RPL>
 struct __align__(16) ClShared {
-  float slot[2][kClMaxCta][32];  // partial dots, [parity][source CTA][column]
+  float slot[2][kClMaxCta][kClSlotLd];  // partial dots, [parity][source CTA][column]
   float rowv[2][32];             // panel row j, [parity][column] (pushed by CTA 0)
   float xs[2][32 * RPL];         // pivot column published by its owner, [parity][row]
   uint64_t mbar[2];
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
   cl_barrier_wait();
 
   const bool top = (p == 0);  // the CTA holding panel rows 0 .. 31 (every pivot row)
-  const uint32_t my_slot_off = (uint32_t)((p * 32 + 4 * g) * sizeof(float));
+  const uint32_t my_slot_off = (uint32_t)((p * kClSlotLd + 4 * g) * sizeof(float));
   const int src = lane & 15;  // source CTA whose partials this lane adds (lanes 16.. repeat 0..15)
   bool ok = true;
   for (int j = 0; j < jmax; ++j) {
