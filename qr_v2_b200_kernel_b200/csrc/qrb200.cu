@@ -665,6 +665,16 @@ static bool wy4_enabled() {
   }
   return v == 1;
 }
+// QRB200_NARROW_TILES=0 keeps 128-column V^T C tiles and 64 x 64 update tiles for updates of
+// 32 or 64 columns.
+static bool narrow_tiles() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_NARROW_TILES");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
 // QRB200_VTC8X8=1 selects the 8 x 8-per-thread V^T C kernel (measured slower on B200 than the
 // 8 x 4 one at C3 and C5, so off by default).
 static bool wy_vtc8x8() {
@@ -722,7 +732,14 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_vtc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(wy_upd3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpd3Smem);
+        e = cudaFuncSetAttribute(wy_upd3_kernel<kU3Rows, kU3Cols>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)upd3_smem<kU3Rows, kU3Cols>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_upd3_kernel<128, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)upd3_smem<128, 32>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_vtcn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcn_smem<32>());
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(wy_vtcn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcn_smem<64>());
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_vtc4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
       if (e == cudaSuccess)
@@ -767,7 +784,14 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
         wy_vtc3_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 256, kVtc3Smem, s>>>(wp);
     }
     else
-      wy_vtc2_kernel<<<dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), 256, kVtc2Smem, s>>>(wp);
+    {
+      if (ncl <= 32 && narrow_tiles())
+        wy_vtcn_kernel<32><<<dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), 256, vtcn_smem<32>(), s>>>(wp);
+      else if (ncl <= 64 && narrow_tiles())
+        wy_vtcn_kernel<64><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, vtcn_smem<64>(), s>>>(wp);
+      else
+        wy_vtc2_kernel<<<dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), 256, kVtc2Smem, s>>>(wp);
+    }
   } else {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
     wy_vtc_kernel<kNB><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
@@ -787,10 +811,17 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       const int grid = (int)std::min<long long>(nt, 2LL * num_sms());
       wy_upd4_kernel<<<grid, 256, kUpd4Smem, s>>>(wp, tc, tr, (int)nt);
     } else if (vec && wy3_enabled()) {
-      const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
-      const long long nt = (long long)tc * tr * batch;
-      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-      wy_upd3_kernel<<<grid, 256, kUpd3Smem, s>>>(wp, tc, tr, (int)nt);
+      if (ncl <= 32 && narrow_tiles()) {
+        const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
+        const long long nt = (long long)tc * tr * batch;
+        const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+        wy_upd3_kernel<128, 32><<<grid, 256, upd3_smem<128, 32>(), s>>>(wp, tc, tr, (int)nt);
+      } else {
+        const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
+        const long long nt = (long long)tc * tr * batch;
+        const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+        wy_upd3_kernel<kU3Rows, kU3Cols><<<grid, 256, upd3_smem<kU3Rows, kU3Cols>(), s>>>(wp, tc, tr, (int)nt);
+      }
     } else if (vec)
       wy_upd2_kernel<<<dim3(cdiv(ncl, kU2Cols), cdiv(m, kU2Rows), (unsigned)batch), 256, 0, s>>>(wp);
     else

@@ -282,52 +282,57 @@ __global__ void __launch_bounds__(256) wy_vtc3_kernel(WyParams P) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Persistent C <- C - V W2 over 64 x 64 tiles: each CTA walks tiles blockIdx.x, + gridDim.x,
-// ..., with the next tile's C, V and W2 slices already streaming into the other half of a
-// two-stage cp.async ring while the current one is computed (4 x 4 outputs per thread; three
-// CTAs per SM).
-constexpr int kU3Rows = 64, kU3Cols = 64;
+// Persistent C <- C - V W2 over TR x TC tiles (64 x 64, or 128 x 32 for the narrowest
+// updates): each CTA walks tiles blockIdx.x, + gridDim.x, ..., with the next tile's C, V and W2
+// slices already streaming into the other half of a two-stage cp.async ring while the current
+// one is computed (4 x 4 outputs per thread, paired FMAs).
+template <int TR, int TC>
 struct Upd3Stage {
-  float C[kU3Rows][kU3Cols];
-  float V[kU3Rows][32 + 4];
-  float W[32][kU3Cols];
+  float C[TR][TC];
+  float V[TR][32 + 4];
+  float W[32][TC];
 };
-constexpr size_t kUpd3Smem = sizeof(Upd3Stage) * 2;
+constexpr int kU3Rows = 64, kU3Cols = 64;
+template <int TR, int TC>
+constexpr size_t upd3_smem() { return sizeof(Upd3Stage<TR, TC>) * 2; }
 
+template <int TR, int TC>
 __global__ void __launch_bounds__(256) wy_upd3_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+  static_assert(TR * TC == 4096, "256 threads x 4 x 4 outputs");
+  constexpr int CG = TC / 4;  // column groups of 4
   extern __shared__ __align__(16) unsigned char u3_smem_raw[];
-  Upd3Stage* st = reinterpret_cast<Upd3Stage*>(u3_smem_raw);
+  Upd3Stage<TR, TC>* st = reinterpret_cast<Upd3Stage<TR, TC>*>(u3_smem_raw);
   const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
-  const int tid = threadIdx.x, cg = tid & 15, rg = tid >> 4;
+  const int tid = threadIdx.x, cg = tid % CG, rg = tid / CG;
   auto tile_of = [&](int t, int& b, int& row0, int& col0) {
     const int per_b = tiles_c * tiles_r;
     b = t / per_b;
     const int rem = t - b * per_b;
-    row0 = (rem / tiles_c) * kU3Rows;
-    col0 = P.coff + (rem % tiles_c) * kU3Cols;
+    row0 = (rem / tiles_c) * TR;
+    col0 = P.coff + (rem % tiles_c) * TC;
   };
   auto issue = [&](int t, int slot) {
     int b, row0, col0;
     tile_of(t, b, row0, col0);
-    Upd3Stage& s = st[slot];
+    Upd3Stage<TR, TC>& s = st[slot];
     const float* __restrict__ Sb = P.src + (long long)b * P.src_bstride;
     const float* __restrict__ Hb = P.H + (long long)b * n * n;
     const float* __restrict__ W2b = P.W2 + (long long)b * 32 * P.ncmax;
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {  // C: 64 rows x 16 float4
-      const int e = it * 256 + tid, rr = e >> 4, q = e & 15, r = row0 + rr, col = col0 + 4 * q;
+    for (int it = 0; it < TR * CG / 256; ++it) {  // C: TR rows x CG float4
+      const int e = it * 256 + tid, rr = e / CG, q = e % CG, r = row0 + rr, col = col0 + 4 * q;
       const bool ok = r < m && col < nc;
       cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
     }
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {  // V: 64 rows x 8 float4
+    for (int it = 0; it < TR * 8 / 256; ++it) {  // V: TR rows x 8 float4
       const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = row0 + rr;
       const bool ok = r < m && 4 * q < w;
       cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
     }
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {  // W2: 32 rows x 16 float4
-      const int e = it * 256 + tid, c = e >> 4, q = e & 15, col = col0 + 4 * q;
+    for (int it = 0; it < 32 * CG / 256; ++it) {  // W2: 32 rows x CG float4
+      const int e = it * 256 + tid, c = e / CG, q = e % CG, col = col0 + 4 * q;
       const bool ok = col < nc;
       cp_async16(&s.W[c][4 * q], ok ? W2b + (long long)c * P.ncmax + col : W2b, ok);
     }
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(256) wy_upd3_kernel(WyParams P, int tiles_c, i
     __syncthreads();
     int b, row0, col0;
     tile_of(t, b, row0, col0);
-    Upd3Stage& s = st[slot];
+    Upd3Stage<TR, TC>& s = st[slot];
     if (row0 == 0) {
       // Panel rows 0..31: V is unit lower triangular there.
 #pragma unroll
@@ -393,6 +398,115 @@ __global__ void __launch_bounds__(256) wy_upd3_kernel(WyParams P, int tiles_c, i
     __syncthreads();  // the slot is refilled by the next iteration's issue
   }
   cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------------------
+// V^T C for narrow updates (COLS = 32 or 64 trailing columns): the 32 x COLS outputs of a CTA
+// are 4 x 4 per thread, and the 128 / COLS thread phases take alternate rows of every 32-row
+// stage (so no thread works on padding columns); the phase partials are added in shared
+// memory in phase order at the end. Stages as wy_vtc2_kernel.
+template <int COLS>
+struct VtcnStage {
+  float C[kV2Rows][COLS];
+  float V[kV2Rows][32];
+};
+template <int COLS>
+constexpr size_t vtcn_smem() { return sizeof(VtcnStage<COLS>) * kV2Stages + (size_t)(128 / COLS) * 32 * COLS * 4; }
+
+template <int COLS>
+__global__ void __launch_bounds__(256) wy_vtcn_kernel(WyParams P) {
+  constexpr int CG = COLS / 4, NPH = 128 / COLS;
+  extern __shared__ __align__(16) unsigned char vn_smem_raw[];
+  VtcnStage<COLS>* st = reinterpret_cast<VtcnStage<COLS>*>(vn_smem_raw);
+  float* red = reinterpret_cast<float*>(vn_smem_raw + sizeof(VtcnStage<COLS>) * kV2Stages);  // [NPH][32][COLS]
+  const int bidx = blockIdx.z, split = blockIdx.y;
+  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
+  const int col0 = P.coff + blockIdx.x * COLS;
+  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
+  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
+  const int tid = threadIdx.x, tx = tid % CG, ty = (tid / CG) % 8, ph = tid / (CG * 8);
+  const int r_begin = split * P.rows_per_split;
+  const int r_end = min(n - k, r_begin + P.rows_per_split);
+  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV2Rows - 1) / kV2Rows : 0;
+
+  auto issue = [&](int ch) {
+    VtcnStage<COLS>& s = st[ch % kV2Stages];
+    const int rb = r_begin + ch * kV2Rows;
+#pragma unroll
+    for (int it = 0; it < kV2Rows * CG / 256; ++it) {  // C: 32 rows x CG float4
+      const int e = it * 256 + tid, rr = e / CG, q = e % CG, r = rb + rr, col = col0 + 4 * q;
+      const bool ok = r < r_end && col < nc;
+      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
+    }
+    {  // V: 32 rows x 8 float4
+      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
+      const bool ok = r < r_end && 4 * q < w;
+      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
+    }
+  };
+
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+#pragma unroll
+  for (int s = 0; s < kV2Stages - 1; ++s) {
+    if (s < nchunks) issue(s);
+    cp_async_commit();
+  }
+  for (int ch = 0; ch < nchunks; ++ch) {
+    cp_async_wait<kV2Stages - 2>();
+    __syncthreads();
+    if (ch + kV2Stages - 1 < nchunks) issue(ch + kV2Stages - 1);
+    cp_async_commit();
+    VtcnStage<COLS>& s = st[ch % kV2Stages];
+    if (split == 0 && ch == 0) {
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int e = it * 256 + tid, rr = e >> 5, c = e & 31;
+        const float v = s.V[rr][c];
+        s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
+      }
+      __syncthreads();
+    }
+#pragma unroll 4
+    for (int rr = ph; rr < kV2Rows; rr += NPH) {
+      const float4 v = *reinterpret_cast<const float4*>(&s.V[rr][4 * ty]);
+      const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * tx]);
+      const float vv[4] = {v.x, v.y, v.z, v.w}, cc[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], cc[e], acc[i][e]);
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<float4*>(&red[(ph * 32 + 4 * ty + i) * COLS + 4 * tx]) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  __syncthreads();
+  // Threads of phase 0 add the phases in order and store.
+  if (ph == 0) {
+    const int col = col0 + 4 * tx;
+    if (col < nc) {
+      float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float4 sum = *reinterpret_cast<const float4*>(&red[(4 * ty + i) * COLS + 4 * tx]);
+#pragma unroll
+        for (int q = 1; q < NPH; ++q) {
+          const float4 x = *reinterpret_cast<const float4*>(&red[(q * 32 + 4 * ty + i) * COLS + 4 * tx]);
+          sum.x += x.x;
+          sum.y += x.y;
+          sum.z += x.z;
+          sum.w += x.w;
+        }
+        *reinterpret_cast<float4*>(out + (long long)(4 * ty + i) * P.ncmax + col) = sum;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------
