@@ -77,11 +77,13 @@ __device__ __forceinline__ void panel_stage_in(const float* __restrict__ S, int 
     stage[(c + 3) * ld + r] = x.w;
   }
 }
+// t0 / nthreads: this thread's index among the nthreads threads that share the copy.
 __device__ __forceinline__ void panel_stage_out(float* __restrict__ Hb, int n, int k, int r0, int rows,
-                                                int rows_valid, int w, const float* stage, int nthreads) {
+                                                int rows_valid, int w, const float* stage, int nthreads,
+                                                int t0 = -1) {
   const int ld = rows + 1;
   const bool vec = ((n & 3) == 0) && ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(Hb) & 15u) == 0);
-  for (int idx = threadIdx.x; idx < rows * 8; idx += nthreads) {
+  for (int idx = (t0 < 0 ? (int)threadIdx.x : t0); idx < rows * 8; idx += nthreads) {
     const int r = idx >> 3, q = idx & 7, c = 4 * q;
     if (r >= rows_valid || c >= w) continue;
     const float4 x = make_float4(stage[(c + 0) * ld + r], stage[(c + 1) * ld + r], stage[(c + 2) * ld + r],
@@ -340,10 +342,7 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
       }
     }
   }
-  if (HAS_T) {
-    __syncthreads();
-    if (g == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
-  }
+  // T (from sh.G and sh.tau) is built by the caller, after its next CTA barrier.
 }
 
 // Two CTAs per SM for the 8-warp shape (<= 128 registers), so one CTA's reflector latency
@@ -374,18 +373,25 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_own
   }
   __syncthreads();
   factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
-  __syncthreads();
+  __syncthreads();  // every warp is done reading the stage
 #pragma unroll
   for (int q = 0; q < CPW; ++q) {
     const int c = g + NW * q;
 #pragma unroll
     for (int i = 0; i < RPL; ++i) stage[c * (R + 1) + lane + 32 * i] = a[q][i];
   }
-  __syncthreads();
-  panel_stage_out(Hb, n, k, 0, R, min(R, m), w, stage, 32 * NW);
-  if (HAS_T && P.T != nullptr) {
-    float* Tb = P.T + (long long)bidx * P.t_bstride;
-    for (int i = threadIdx.x; i < 32 * 32; i += 32 * NW) Tb[i] = sh.T[i / 32][i % 32];
+  __syncthreads();  // staged panel, Gram entries and tau are complete
+  if (HAS_T && g == 0) {
+    // Warp 0 builds and stores T while the other warps write the panel.
+    larft_inverse_warp(sh.T, sh.G, sh.tau, min(w, m));
+    __syncwarp();
+    if (P.T != nullptr) {
+      float* Tb = P.T + (long long)bidx * P.t_bstride;
+      for (int i = lane; i < 32 * 32; i += 32) Tb[i] = sh.T[i / 32][i % 32];
+    }
+  } else {
+    const int t0 = HAS_T ? (int)threadIdx.x - 32 : (int)threadIdx.x;
+    panel_stage_out(Hb, n, k, 0, R, min(R, m), w, stage, HAS_T ? 32 * NW - 32 : 32 * NW, t0);
   }
 }
 

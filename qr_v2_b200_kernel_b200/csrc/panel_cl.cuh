@@ -272,20 +272,25 @@ __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
   // Exit barrier split around the write-out: every push into this CTA has landed once its last
   // wait returned, and no CTA leaves before every CTA got that far.
   cl_barrier_arrive();
-  __syncthreads();
-  if (top && g == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
 #pragma unroll
   for (int q = 0; q < 4; ++q)
 #pragma unroll
     for (int i = 0; i < RPL; ++i) stage[(4 * g + q) * (R + 1) + lane + 32 * i] = a[q][i];
-  __syncthreads();
-  if (ok) {
-    panel_stage_out(Hb, n, k, r0, R, rows_valid, w, stage, kClThreads);
-    if (top && threadIdx.x < jmax) tau_out[threadIdx.x] = sh.tau[threadIdx.x];
-    if (P.T != nullptr && top) {
-      float* Tb = P.T + (long long)bidx * P.t_bstride;
-      for (int i = threadIdx.x; i < 32 * 32; i += kClThreads) Tb[i] = sh.T[i / 32][i % 32];
+  __syncthreads();  // the staged panel, tau and the Gram entries are complete
+  if (top && g == 0) {
+    // Warp 0 of the top CTA builds and stores T and tau while the other warps write the panel.
+    larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
+    __syncwarp();
+    if (ok) {
+      if (lane < jmax) tau_out[lane] = sh.tau[lane];
+      if (P.T != nullptr) {
+        float* Tb = P.T + (long long)bidx * P.t_bstride;
+        for (int i = lane; i < 32 * 32; i += 32) Tb[i] = sh.T[i / 32][i % 32];
+      }
     }
+  } else if (ok) {
+    const int t0 = top ? (int)threadIdx.x - 32 : (int)threadIdx.x;
+    panel_stage_out(Hb, n, k, r0, R, rows_valid, w, stage, top ? kClThreads - 32 : kClThreads, t0);
   }
   cl_barrier_wait();
 }

@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(kPanelThreads) small_qr_kernel(const float* __
     for (int e = tid; e < 32 * 33; e += NT) (&sh.ps.T[0][0])[e] = 0.f;
     __syncthreads();
     factor_panel_owner<RPL, 1, true>(a, w, w, sh.ps, taub + k);
+    __syncthreads();
+    if (warp == 0) larft_inverse_warp(sh.ps.T, sh.ps.G, sh.ps.tau, w);
     if (warp < w) {
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
