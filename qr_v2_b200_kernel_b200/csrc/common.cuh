@@ -17,6 +17,16 @@ __device__ __forceinline__ void named_arrive(int id, int nthreads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Programmatic dependent launch: let the next kernel in the stream be scheduled now, and wait
+// until every kernel this one depends on has finished and its writes are visible. A kernel
+// starts with both (before its first global read), so a launch with the programmatic
+// serialisation attribute only overlaps launch latency; without that attribute they return at
+// once.
+__device__ __forceinline__ void griddep_launch_wait() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Transposed butterfly reduction of NV per-lane partial sums across a warp.
 // On return d[0 .. NV/32) of lane L hold the warp-wide sums of the original entries
 // L*(NV/32) + q. Each of the five xor steps halves the live array: the lane keeps the

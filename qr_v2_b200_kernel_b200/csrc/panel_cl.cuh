@@ -111,6 +111,7 @@ __device__ __forceinline__ void cl_barrier_wait() {
 // a release arrive of every pushing lane.
 template <int RPL, bool ASYNC>
 __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
+  griddep_launch_wait();
   constexpr int R = 32 * RPL;
   __shared__ ClShared<RPL> sh;
   extern __shared__ __align__(16) unsigned char cl_smem_raw[];

@@ -187,6 +187,7 @@ __device__ __forceinline__ void panel_fw_t_step(PanelFwShared<RPL>& sh, int b) {
 
 template <int RPL>
 __global__ void __launch_bounds__(32 * kPanelFwWarps) panel_fw_kernel(PanelParams P) {
+  griddep_launch_wait();
   constexpr int R = 32 * RPL, RPG = R / 8;
   extern __shared__ __align__(16) unsigned char pfw_smem_raw[];
   PanelFwShared<RPL>& sh = *reinterpret_cast<PanelFwShared<RPL>*>(pfw_smem_raw);

@@ -204,6 +204,46 @@ static int check_device() {
   return QRB200_ERR_DEVICE;
 }
 
+// QRB200_PDL=0 launches the single-level chain kernels without programmatic dependent launch.
+static bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_PDL");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Launch with an optional cluster shape and, for kernels that begin with griddep_launch_wait(),
+// programmatic dependent launch (the kernel may be scheduled while its predecessor in the
+// stream finishes; it waits for it before touching global memory).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            unsigned cluster, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (cluster > 0) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl && pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int RPL, bool HAS_T>
 static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
   static PerDevice configured;
@@ -341,8 +381,8 @@ static cudaError_t launch_fw(const PanelParams& pp, long long batch, cudaStream_
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  panel_fw_kernel<RPL><<<dim3(1, (unsigned)batch), 32 * kPanelFwWarps, panel_fw_smem<RPL>(), s>>>(pp);
-  return cudaGetLastError();
+  return launch_k(panel_fw_kernel<RPL>, dim3(1, (unsigned)batch), dim3(32 * kPanelFwWarps), panel_fw_smem<RPL>(), s, 0,
+                  true, pp);
 }
 
 template <int RPL, bool ASYNC>
@@ -357,19 +397,8 @@ static cudaError_t launch_cl(const PanelParams& pp, int cluster, long long batch
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
-  cfg.blockDim = dim3(kClThreads, 1, 1);
-  cfg.dynamicSmemBytes = panel_cl_smem<RPL>();
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, panel_cl_kernel<RPL, ASYNC>, pp);
+  return launch_k(panel_cl_kernel<RPL, ASYNC>, dim3((unsigned)cluster, (unsigned)batch, 1), dim3(kClThreads, 1, 1),
+                  panel_cl_smem<RPL>(), s, (unsigned)cluster, true, pp);
 }
 
 // Rows per CTA of the cluster panel (QRB200_CL_ROWS = 128, 256 or 512; 0 turns the cluster
@@ -722,6 +751,7 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   wp.ncmax = n;
   wp.coff = coff;
   const double bm = (double)batch * m;
+  cudaError_t ep = cudaSuccess;  // first launch error of the three kernels
   const bool vec = wy2_enabled() && w == kNB && (n % 4) == 0 && (sbs % 4) == 0 &&
                    ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(H)) & 15u) == 0;
   if (vec) {
@@ -760,19 +790,8 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     }
     const int cp = cdiv(m, kU1Rows);
     LaunchScope ls(K_U1, 4.0 * bm * w * ncl + (double)batch * w * w * ncl, 12.0 * bm * ncl + 4.0 * bm * w);
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch);
-    cfg.blockDim = dim3(256, 1, 1);
-    cfg.dynamicSmemBytes = kU1Smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)cp;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, wy_u1_kernel, wp);
+    return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(256), kU1Smem, s,
+                    (unsigned)cp, true, wp);
   }
   if (vec) {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
@@ -781,16 +800,16 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       if (wy_vtc8x8())
         wy_vtc4_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 128, kVtc3Smem, s>>>(wp);
       else
-        wy_vtc3_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 256, kVtc3Smem, s>>>(wp);
+        ep = launch_k(wy_vtc3_kernel, dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc3Smem, s, 0, true, wp);
     }
     else
     {
       if (ncl <= 32 && narrow_tiles())
-        wy_vtcn_kernel<32><<<dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), 256, vtcn_smem<32>(), s>>>(wp);
+        ep = launch_k(wy_vtcn_kernel<32>, dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<32>(), s, 0, true, wp);
       else if (ncl <= 64 && narrow_tiles())
-        wy_vtcn_kernel<64><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, vtcn_smem<64>(), s>>>(wp);
+        ep = launch_k(wy_vtcn_kernel<64>, dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<64>(), s, 0, true, wp);
       else
-        wy_vtc2_kernel<<<dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), 256, kVtc2Smem, s>>>(wp);
+        ep = launch_k(wy_vtc2_kernel, dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc2Smem, s, 0, true, wp);
     }
   } else {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
@@ -799,7 +818,7 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   {
     LaunchScope ls(K_TW, (double)batch * w * w * ncl, 4.0 * batch * (wp.nsplit + 1.0) * w * ncl);
     if (vec)
-      wy_tw2_kernel<<<dim3(cdiv(ncl, 32), (unsigned)batch), 256, 0, s>>>(wp);
+      ep = launch_k(wy_tw2_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp);
     else
       wy_tw_kernel<kNB><<<dim3(cdiv(ncl, 128), (unsigned)batch), 128, 0, s>>>(wp);
   }
@@ -809,25 +828,25 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       const int tc = cdiv(ncl, kU4Cols), tr = cdiv(m, kU4Rows);
       const long long nt = (long long)tc * tr * batch;
       const int grid = (int)std::min<long long>(nt, 2LL * num_sms());
-      wy_upd4_kernel<<<grid, 256, kUpd4Smem, s>>>(wp, tc, tr, (int)nt);
+      ep = launch_k(wy_upd4_kernel, dim3(grid), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt);
     } else if (vec && wy3_enabled()) {
       if (ncl <= 32 && narrow_tiles()) {
         const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
         const long long nt = (long long)tc * tr * batch;
         const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        wy_upd3_kernel<128, 32><<<grid, 256, upd3_smem<128, 32>(), s>>>(wp, tc, tr, (int)nt);
+        ep = launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt);
       } else {
         const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
         const long long nt = (long long)tc * tr * batch;
         const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        wy_upd3_kernel<kU3Rows, kU3Cols><<<grid, 256, upd3_smem<kU3Rows, kU3Cols>(), s>>>(wp, tc, tr, (int)nt);
+        ep = launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt);
       }
     } else if (vec)
       wy_upd2_kernel<<<dim3(cdiv(ncl, kU2Cols), cdiv(m, kU2Rows), (unsigned)batch), 256, 0, s>>>(wp);
     else
       wy_upd_kernel<kNB><<<dim3(cdiv(ncl, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
   }
-  return cudaGetLastError();
+  return ep != cudaSuccess ? ep : cudaGetLastError();
 }
 
 // Look-ahead streams of one device: the critical chain (panels, narrow updates, T, Y and the

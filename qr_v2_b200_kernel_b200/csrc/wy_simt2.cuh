@@ -37,6 +37,7 @@ struct Vtc2Stage {
 constexpr size_t kVtc2Smem = sizeof(Vtc2Stage) * kV2Stages;
 
 __global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
+  griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char v2_smem_raw[];
   Vtc2Stage* st = reinterpret_cast<Vtc2Stage*>(v2_smem_raw);
   const int bidx = blockIdx.z, split = blockIdx.y;
@@ -196,6 +197,7 @@ struct Vtc3Stage {
 constexpr size_t kVtc3Smem = sizeof(Vtc3Stage) * kV3Stages;
 
 __global__ void __launch_bounds__(256) wy_vtc3_kernel(WyParams P) {
+  griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char v3_smem_raw[];
   Vtc3Stage* st = reinterpret_cast<Vtc3Stage*>(v3_smem_raw);
   const int bidx = blockIdx.z, split = blockIdx.y;
@@ -298,6 +300,7 @@ constexpr size_t upd3_smem() { return sizeof(Upd3Stage<TR, TC>) * 2; }
 
 template <int TR, int TC>
 __global__ void __launch_bounds__(256) wy_upd3_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+  griddep_launch_wait();
   static_assert(TR * TC == 4096, "256 threads x 4 x 4 outputs");
   constexpr int CG = TC / 4;  // column groups of 4
   extern __shared__ __align__(16) unsigned char u3_smem_raw[];
@@ -415,6 +418,7 @@ constexpr size_t vtcn_smem() { return sizeof(VtcnStage<COLS>) * kV2Stages + (siz
 
 template <int COLS>
 __global__ void __launch_bounds__(256) wy_vtcn_kernel(WyParams P) {
+  griddep_launch_wait();
   constexpr int CG = COLS / 4, NPH = 128 / COLS;
   extern __shared__ __align__(16) unsigned char vn_smem_raw[];
   VtcnStage<COLS>* st = reinterpret_cast<VtcnStage<COLS>*>(vn_smem_raw);
@@ -514,6 +518,7 @@ __global__ void __launch_bounds__(256) wy_vtcn_kernel(WyParams P) {
 // partials of W rows 4 g .. 4 g + 3 (independent, coalesced loads), then forms the same rows
 // of T^T W from shared memory.
 __global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
+  griddep_launch_wait();
   __shared__ float Ts[32][33];
   __shared__ float Ws[32][33];
   const int bidx = blockIdx.y;
@@ -666,6 +671,7 @@ struct Upd4Stage {
 constexpr size_t kUpd4Smem = sizeof(Upd4Stage) * 2;
 
 __global__ void __launch_bounds__(256) wy_upd4_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+  griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char u4_smem_raw[];
   Upd4Stage* st = reinterpret_cast<Upd4Stage*>(u4_smem_raw);
   const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;

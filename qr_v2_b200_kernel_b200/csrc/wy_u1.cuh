@@ -44,6 +44,7 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
 }
 
 __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
+  griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char u1_smem_raw[];
   U1Shared& sh = *reinterpret_cast<U1Shared*>(u1_smem_raw);
   uint32_t CP, p;
