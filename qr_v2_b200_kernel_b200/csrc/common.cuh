@@ -95,4 +95,31 @@ __device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnor
   return r;
 }
 
+// Squared norms below 2^-100 (tail entries below about 2^-50) are sums of squares near or
+// inside the subnormal range, which keep fewer than 24 bits: tau then disagrees with its
+// vector and Q loses orthogonality. Such a reflector is rebuilt from the pivot and the squared
+// tail norm of the tail scaled by 2^100, the way LAPACK's slarfg rescales small columns. tau is
+// scale invariant; diag scales down and scale up by the same power of two, both exactly. A
+// column whose scaled scale still overflows (every entry subnormal) gets no reflector.
+// The caller's test is uniform across the warp that reduced the norm (xor-butterfly sums are
+// the same in every lane), so the rare rescaled sum costs one branch on ordinary data.
+constexpr float kRescaleUp = 0x1p100f, kRescaleDown = 0x1p-100f;
+
+__device__ __forceinline__ bool reflector_needs_rescale(float alpha, float xnorm2) {
+  return fmaf(alpha, alpha, xnorm2) < kRescaleDown;
+}
+
+// xnorm2_up: the squared tail norm of the tail multiplied by kRescaleUp.
+__device__ __forceinline__ Reflector make_reflector_rescaled(float alpha, float xnorm2_up) {
+  Reflector r = make_reflector(alpha * kRescaleUp, xnorm2_up);
+  r.diag *= kRescaleDown;
+  r.scale *= kRescaleUp;
+  if (!(fabsf(r.scale) <= 3.0e38f)) {
+    r.diag = alpha;
+    r.tau = 0.f;
+    r.scale = 0.f;
+  }
+  return r;
+}
+
 }  // namespace qrb200

@@ -294,7 +294,20 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
       const float alpha = __shfl_sync(kFullMask, x[0], j);
-      const Reflector rf = make_reflector_fast(alpha, s);
+      Reflector rf;
+      if (reflector_needs_rescale(alpha, s)) {
+        float su = 0.f;
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+          const float xu = (lane + 32 * i > j) ? x[i] * kRescaleUp : 0.f;
+          su = fmaf(xu, xu, su);
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) su += __shfl_xor_sync(kFullMask, su, o);
+        rf = make_reflector_rescaled(alpha, su);
+      } else {
+        rf = make_reflector_fast(alpha, s);
+      }
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
         const int lr = lane + 32 * i;

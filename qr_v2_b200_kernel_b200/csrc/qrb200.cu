@@ -286,6 +286,19 @@ static cudaError_t launch_small(const float* A, float* H, float* tau, long long 
   return cudaGetLastError();
 }
 
+// Pause (ns) between the update warps' polls in the whole-matrix kernel (QRB200_FW_POLL_NS,
+// default 50): idle update warps that sleep leave issue slots to the factor warp, whose
+// reflector chain is the kernel's critical path (about 3% faster on C1 than busy polling).
+static int fw_poll_ns() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_FW_POLL_NS");
+    v = e ? atoi(e) : 50;
+    if (v < 0 || v > 1000) v = 50;
+  }
+  return v;
+}
+
 template <int NMAX, int NWL>
 static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long long batch, int n, long long abs,
                                    cudaStream_t s) {
@@ -297,7 +310,7 @@ static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long lo
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n);
+  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n, fw_poll_ns());
   return cudaGetLastError();
 }
 

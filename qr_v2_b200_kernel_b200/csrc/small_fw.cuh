@@ -56,6 +56,17 @@ __device__ __forceinline__ bool fw_wait_geq_sleep(const int* p, int v) {
   return false;
 }
 
+// As fw_wait_geq with a short pause of ns nanoseconds between polls (update warps: fewer
+// shared-memory polls competing with the factor warp); at most 2^22 polls.
+__device__ __forceinline__ bool fw_wait_geq_pause(const int* p, int v, int ns) {
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    if (ld_acquire_cta(p) >= v) return true;
+    __nanosleep(ns);
+  }
+  atomicExch(&g_device_status, kDevStatusHandoffTimeout);
+  return false;
+}
+
 // Publish by lane 0 after every lane's shared-memory writes.
 __device__ __forceinline__ void fw_publish(int* p, int v) {
   __threadfence_block();
@@ -102,7 +113,20 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
     for (int o = 16; o >= 1; o >>= 1)
 #pragma unroll
       for (int c = 0; c < CPW; ++c) d[c] += __shfl_xor_sync(kFullMask, d[c], o);
-    const Reflector rf = make_reflector_fast(rowj[jj], d[jj]);
+    Reflector rf;
+    if (reflector_needs_rescale(rowj[jj], d[jj])) {
+      float su = 0.f;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        const float xu = xm[i] * kRescaleUp;
+        su = fmaf(xu, xu, su);
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) su += __shfl_xor_sync(kFullMask, su, o);
+      rf = make_reflector_rescaled(rowj[jj], su);
+    } else {
+      rf = make_reflector_fast(rowj[jj], d[jj]);
+    }
     float z[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
@@ -258,7 +282,8 @@ constexpr size_t small_fw_smem() { return sizeof(SmallFwShared<NMAX, 4>); }
 // NWL warps are launched: the factor warp, idle warps 4, 8, .. and NU update warps.
 template <int NMAX, int NWL>
 __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restrict__ A, long long a_bstride,
-                                                            float* __restrict__ H, float* __restrict__ tau, int n) {
+                                                            float* __restrict__ H, float* __restrict__ tau, int n,
+                                                            int P_SLEEP_NS = 0) {
   constexpr int CPW = 4;
   constexpr int RPL = NMAX / 32;               // factor-warp rows per lane
   constexpr int RPG = NMAX / 8;                // update-warp rows per lane
@@ -366,7 +391,7 @@ __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restr
       x[k] = (r < n && col < n) ? Ab[(long long)r * n + col] : 0.f;
     }
     for (int s = 0; s <= t - 2; ++s) {
-      if (!fw_wait_geq(&sh.vcount, s + 1)) return;
+      if (!(P_SLEEP_NS > 0 ? fw_wait_geq_pause(&sh.vcount, s + 1, P_SLEEP_NS) : fw_wait_geq(&sh.vcount, s + 1))) return;
       fw_apply_rows<NMAX, CPW, RPG>(x, &sh.V[s][0][0], &sh.T[s][0][0], g4);
     }
     // Slot t & 1 last held block t - 2, which the factor warp read before publishing V_{t-2}:

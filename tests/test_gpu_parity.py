@@ -91,14 +91,15 @@ def test_reference_test_cases(idx):
 
 def test_edge_matrices():
     n = 96
+    g = torch.Generator().manual_seed(96)
     cases = {
         "zero": torch.zeros(2, n, n),
         "identity": torch.eye(n).expand(2, n, n).clone(),
         "neg_identity": -torch.eye(n).expand(2, n, n).clone(),
-        "zero_column": torch.randn(2, n, n).index_fill_(2, torch.tensor([5, 40]), 0.0),
-        "rank_one": torch.randn(2, n, 1) @ torch.randn(2, 1, n),
-        "tiny": torch.randn(2, n, n) * 1e-20,
-        "huge": torch.randn(2, n, n) * 1e15,
+        "zero_column": torch.randn(2, n, n, generator=g).index_fill_(2, torch.tensor([5, 40]), 0.0),
+        "rank_one": torch.randn(2, n, 1, generator=g) @ torch.randn(2, 1, n, generator=g),
+        "tiny": torch.randn(2, n, n, generator=g) * 1e-20,
+        "huge": torch.randn(2, n, n, generator=g) * 1e15,
     }
     for name, A in cases.items():
         A = A.float().cuda().contiguous()
@@ -108,6 +109,21 @@ def test_edge_matrices():
     # the zero matrix: every reflector is the identity
     H, tau = _run(torch.zeros(1, 40, 40, device="cuda"))
     assert (tau == 0).all() and (H == 0).all()
+
+
+@pytest.mark.parametrize("n", [96, 200, 600])
+def test_tiny_scale_keeps_q_orthogonal(n):
+    """Entries near 1e-20 square into fp32's subnormal range (fewer than 24 bits), which left
+    tau inconsistent with its vector on short column tails; the rescaled reflector keeps Q
+    orthogonal. n = 96: whole-matrix kernel; 200: owner panels; 600: cluster panels (tails of
+    513+ rows, whose sums stay accurate at 1e-20) and factor-warp panels. Much smaller entries
+    are out of range: the panels form tail-by-column dot products before normalising the tail
+    (as the reference panel does), and below about 1e-22 those products underflow."""
+    g = torch.Generator().manual_seed(n)
+    A = (torch.randn(3, n, n, generator=g) * 1e-20).cuda()
+    H, tau = _run(A)
+    assert torch.isfinite(H).all() and torch.isfinite(tau).all()
+    _assert_gate(A, H, tau, n)
 
 
 def test_noncontiguous_and_batch_views():
