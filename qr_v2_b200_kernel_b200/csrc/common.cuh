@@ -75,13 +75,46 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float xnorm2) {
   return r;
 }
 
+// Squared norms below 2^-100 (tail entries below about 2^-50) are sums of squares near or
+// inside the subnormal range, which keep fewer than 24 bits: tau then disagrees with its
+// vector and Q loses orthogonality. Such a reflector is rebuilt from the pivot and the squared
+// norm of the tail scaled by 2^100 (xnorm2_up), the way LAPACK's slarfg rescales small
+// columns. tau is scale invariant; diag scales down and scale up by the same power of two,
+// both exactly. A column whose scaled scale still overflows (every entry subnormal) gets no
+// reflector.
+constexpr float kRescaleUp = 0x1p100f, kRescaleDown = 0x1p-100f;
+
+// Out of line: the hot loops keep a plain branch to a call that ordinary inputs never take
+// (inlined, the precise square root and reciprocals of this path slowed the reflector chain).
+__device__ __noinline__ Reflector make_reflector_outside(float alpha, float xnorm2, float xnorm2_up) {
+  if (fmaf(alpha, alpha, xnorm2) < kRescaleDown) {
+    Reflector r = make_reflector(alpha * kRescaleUp, xnorm2_up);
+    r.diag *= kRescaleDown;
+    r.scale *= kRescaleUp;
+    if (!(fabsf(r.scale) <= 3.0e38f)) {
+      r.diag = alpha;
+      r.tau = 0.f;
+      r.scale = 0.f;
+    }
+    return r;
+  }
+  return make_reflector(alpha, xnorm2);
+}
+
 // Reflector scalars as make_reflector, with the square root and the reciprocal from the
 // hardware approximations, the reciprocal square root refined by one Newton step
 // (y <- y (3 - x y^2) / 2): about 1 ulp. Norms outside [1e-30, 1e30] take the correctly
-// rounded path, where the approximations lose range.
-__device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnorm2) {
+// rounded path, where the approximations lose range, rescaled below 2^-100 (xnorm2_up: the
+// squared norm of the tail times 2^200; pass any value when the caller has none, e.g. a
+// cluster-wide norm of 513+ rows, whose sum stays accurate).
+__device__ __forceinline__ bool reflector_fast_range(float alpha, float xnorm2) {
   const float nrm2 = fmaf(alpha, alpha, xnorm2);
-  if (!(nrm2 > 1e-30f && nrm2 < 1e30f)) return make_reflector(alpha, xnorm2);
+  return nrm2 > 1e-30f && nrm2 < 1e30f;
+}
+
+// The fast form alone, for alpha^2 + xnorm2 inside [1e-30, 1e30].
+__device__ __forceinline__ Reflector make_reflector_fast_core(float alpha, float xnorm2) {
+  const float nrm2 = fmaf(alpha, alpha, xnorm2);
   float y = rsqrtf(nrm2);
   y = y * fmaf(-0.5f * nrm2, y * y, 1.5f);
   const float nrm = nrm2 * y;
@@ -95,31 +128,28 @@ __device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnor
   return r;
 }
 
-// Squared norms below 2^-100 (tail entries below about 2^-50) are sums of squares near or
-// inside the subnormal range, which keep fewer than 24 bits: tau then disagrees with its
-// vector and Q loses orthogonality. Such a reflector is rebuilt from the pivot and the squared
-// tail norm of the tail scaled by 2^100, the way LAPACK's slarfg rescales small columns. tau is
-// scale invariant; diag scales down and scale up by the same power of two, both exactly. A
-// column whose scaled scale still overflows (every entry subnormal) gets no reflector.
-// The caller's test is uniform across the warp that reduced the norm (xor-butterfly sums are
-// the same in every lane), so the rare rescaled sum costs one branch on ordinary data.
-constexpr float kRescaleUp = 0x1p100f, kRescaleDown = 0x1p-100f;
-
-__device__ __forceinline__ bool reflector_needs_rescale(float alpha, float xnorm2) {
-  return fmaf(alpha, alpha, xnorm2) < kRescaleDown;
+__device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnorm2, float xnorm2_up) {
+  const float nrm2 = fmaf(alpha, alpha, xnorm2);
+  if (!(nrm2 > 1e-30f && nrm2 < 1e30f)) return make_reflector_outside(alpha, xnorm2, xnorm2_up);
+  float y = rsqrtf(nrm2);
+  y = y * fmaf(-0.5f * nrm2, y * y, 1.5f);
+  const float nrm = nrm2 * y;
+  const float aa = fabsf(alpha);
+  const float inv = __fdividef(1.f, aa + nrm);
+  Reflector r;
+  const bool need = xnorm2 > 0.f;
+  r.diag = need ? (alpha >= 0.f ? -nrm : nrm) : alpha;
+  r.tau = need ? fmaf(aa, y, 1.f) : 0.f;
+  r.scale = need ? (alpha >= 0.f ? inv : -inv) : 0.f;
+  return r;
 }
 
-// xnorm2_up: the squared tail norm of the tail multiplied by kRescaleUp.
-__device__ __forceinline__ Reflector make_reflector_rescaled(float alpha, float xnorm2_up) {
-  Reflector r = make_reflector(alpha * kRescaleUp, xnorm2_up);
-  r.diag *= kRescaleDown;
-  r.scale *= kRescaleUp;
-  if (!(fabsf(r.scale) <= 3.0e38f)) {
-    r.diag = alpha;
-    r.tau = 0.f;
-    r.scale = 0.f;
-  }
-  return r;
+// Callers without the scaled sum (the owner and cluster panels): out of range, the correctly
+// rounded form inline. The owner panel detects norms below 2^-100 itself and refactors the
+// panel scaled; cluster panels (513+ rows per tail) keep the reference's arithmetic.
+__device__ __forceinline__ Reflector make_reflector_fast(float alpha, float xnorm2) {
+  if (!reflector_fast_range(alpha, xnorm2)) return make_reflector(alpha, xnorm2);
+  return make_reflector_fast_core(alpha, xnorm2);
 }
 
 }  // namespace qrb200

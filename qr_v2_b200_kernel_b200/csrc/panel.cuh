@@ -53,28 +53,47 @@ struct PanelParams {
 // `stage` (stage[c * ld + r], ld = rows + 1, so both the transposing writes and the per-column
 // reads are bank-conflict free); each warp then takes its columns from shared memory instead
 // of issuing one 4-byte load per row.
-__device__ __forceinline__ void panel_stage_in(const float* __restrict__ S, int n, int k, int r0, int rows,
-                                               int rows_valid, int w, float* stage, int nthreads) {
-  const int ld = rows + 1;
+// ROWS and NT (the threads sharing the copy, == blockDim.x) are compile-time, so every thread
+// issues up to eight 16-byte loads before its first shared-memory store: a panel load costs
+// one memory latency per eight pieces instead of one per piece.
+template <int ROWS, int NT>
+__device__ __forceinline__ void panel_stage_in(const float* __restrict__ S, int n, int k, int r0, int rows_valid,
+                                               int w, float* stage) {
+  constexpr int LD = ROWS + 1, TOTAL = ROWS * 8;
+  constexpr int ITERS = (TOTAL + NT - 1) / NT;
+  constexpr int B = ITERS < 8 ? ITERS : 8;
   const bool vec = ((n & 3) == 0) && ((k & 3) == 0) && ((reinterpret_cast<uintptr_t>(S) & 15u) == 0);
-  for (int idx = threadIdx.x; idx < rows * 8; idx += nthreads) {
-    const int r = idx >> 3, q = idx & 7, c = 4 * q;
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < rows_valid && c < w) {
-      const float* src = S + (long long)(k + r0 + r) * n + k + c;
-      if (vec && c + 3 < w) {
-        x = *reinterpret_cast<const float4*>(src);
-      } else {
-        x.x = src[0];
-        x.y = (c + 1 < w) ? src[1] : 0.f;
-        x.z = (c + 2 < w) ? src[2] : 0.f;
-        x.w = (c + 3 < w) ? src[3] : 0.f;
+#pragma unroll
+  for (int b0 = 0; b0 < ITERS; b0 += B) {
+    float4 x[B];
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const int idx = (b0 + u) * NT + (int)threadIdx.x;
+      const int r = idx >> 3, c = 4 * (idx & 7);
+      x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (b0 + u < ITERS && idx < TOTAL && r < rows_valid && c < w) {
+        const float* src = S + (long long)(k + r0 + r) * n + k + c;
+        if (vec && c + 3 < w) {
+          x[u] = *reinterpret_cast<const float4*>(src);
+        } else {
+          x[u].x = src[0];
+          x[u].y = (c + 1 < w) ? src[1] : 0.f;
+          x[u].z = (c + 2 < w) ? src[2] : 0.f;
+          x[u].w = (c + 3 < w) ? src[3] : 0.f;
+        }
       }
     }
-    stage[(c + 0) * ld + r] = x.x;
-    stage[(c + 1) * ld + r] = x.y;
-    stage[(c + 2) * ld + r] = x.z;
-    stage[(c + 3) * ld + r] = x.w;
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const int idx = (b0 + u) * NT + (int)threadIdx.x;
+      if (b0 + u < ITERS && idx < TOTAL) {
+        const int r = idx >> 3, c = 4 * (idx & 7);
+        stage[(c + 0) * LD + r] = x[u].x;
+        stage[(c + 1) * LD + r] = x[u].y;
+        stage[(c + 2) * LD + r] = x[u].z;
+        stage[(c + 3) * LD + r] = x[u].w;
+      }
+    }
   }
 }
 // t0 / nthreads: this thread's index among the nthreads threads that share the copy.
@@ -267,6 +286,8 @@ struct OwnerShared {
   float tau[32];
   float G[32][33];
   float T[32][33];
+  int tiny;  // a column's alpha^2 + ||x||^2 fell below 2^-100
+  int amax;  // bits of the panel's largest |entry| (rescaling pass only)
 };
 
 template <int RPL, int CPW, bool HAS_T>
@@ -294,20 +315,8 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
       const float alpha = __shfl_sync(kFullMask, x[0], j);
-      Reflector rf;
-      if (reflector_needs_rescale(alpha, s)) {
-        float su = 0.f;
-#pragma unroll
-        for (int i = 0; i < RPL; ++i) {
-          const float xu = (lane + 32 * i > j) ? x[i] * kRescaleUp : 0.f;
-          su = fmaf(xu, xu, su);
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) su += __shfl_xor_sync(kFullMask, su, o);
-        rf = make_reflector_rescaled(alpha, su);
-      } else {
-        rf = make_reflector_fast(alpha, s);
-      }
+      const Reflector rf = make_reflector_fast(alpha, s);
+      if (lane == 0 && fmaf(alpha, alpha, s) < kRescaleDown) sh.tiny = 1;  // see panel_owner_kernel
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
         const int lr = lane + 32 * i;
@@ -375,7 +384,11 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_own
   float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   if (HAS_T)
     for (int i = threadIdx.x; i < 32 * 33; i += 32 * NW) (&sh.T[0][0])[i] = 0.f;
-  panel_stage_in(S, n, k, 0, R, min(R, m), w, stage, 32 * NW);
+  if (threadIdx.x == 0) {
+    sh.tiny = 0;
+    sh.amax = 0;
+  }
+  panel_stage_in<R, 32 * NW>(S, n, k, 0, min(R, m), w, stage);
   __syncthreads();
   float a[CPW][RPL];
 #pragma unroll
@@ -386,7 +399,43 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_own
   }
   __syncthreads();
   factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
-  __syncthreads();  // every warp is done reading the stage
+  __syncthreads();  // every warp is done reading the stage; sh.tiny is final
+  if (sh.tiny) {
+    // A squared norm fell below 2^-100, where the squares lose digits to the subnormal range
+    // (Q would lose orthogonality). Factor the panel again from its staged input scaled by a
+    // power of two that brings its largest entry near 1, then scale R back: V and tau are
+    // scale invariant and R scales exactly, so this is LAPACK's small-column rescaling done
+    // once per panel. Uniformly small panels (a tiny matrix) are covered; a panel whose
+    // largest entry is ordinary keeps its result. Ordinary inputs never enter this branch.
+    float mx = 0.f;
+#pragma unroll
+    for (int q = 0; q < CPW; ++q)
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) mx = fmaxf(mx, fabsf(stage[(g + NW * q) * (R + 1) + lane + 32 * i]));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
+    if (lane == 0) atomicMax(&sh.amax, __float_as_int(mx));  // non-negative: int order = float order
+    __syncthreads();
+    const float M = __int_as_float(sh.amax);
+    if (M > 0.f && M < 0x1p-40f) {
+      int ex;
+      frexpf(M, &ex);  // M = f 2^ex, f in [0.5, 1)
+      const int up = min(-ex, 126);
+      const float scl = ldexpf(1.f, up), inv = ldexpf(1.f, -up);
+#pragma unroll
+      for (int q = 0; q < CPW; ++q)
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) a[q][i] = stage[(g + NW * q) * (R + 1) + lane + 32 * i] * scl;
+      __syncthreads();
+      factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
+#pragma unroll
+      for (int q = 0; q < CPW; ++q)
+#pragma unroll
+        for (int i = 0; i < RPL; ++i)
+          if (lane + 32 * i <= g + NW * q) a[q][i] *= inv;  // R: rows up to the diagonal
+      __syncthreads();
+    }
+  }
 #pragma unroll
   for (int q = 0; q < CPW; ++q) {
     const int c = g + NW * q;
@@ -428,7 +477,7 @@ __global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams
 
   if (HAS_T)
     for (int i = threadIdx.x; i < 32 * 33; i += kPanelThreads) (&sh.T[0][0])[i] = 0.f;
-  panel_stage_in(S, n, k, r0, R, rows_valid, w, stage, kPanelThreads);
+  panel_stage_in<R, kPanelThreads>(S, n, k, r0, rows_valid, w, stage);
   __syncthreads();
   float a[RPL];
 #pragma unroll

@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
   // mbarriers are initialised.
   cl_barrier_arrive();
   for (int i = threadIdx.x; i < 32 * 33; i += kClThreads) (&sh.T[0][0])[i] = 0.f;
-  panel_stage_in(S, n, k, r0, R, rows_valid, w, stage, kClThreads);
+  panel_stage_in<R, kClThreads>(S, n, k, r0, rows_valid, w, stage);
   __syncthreads();
   float a[4][RPL];
 #pragma unroll

@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? 2 : 1)) panel_la_
     (&sh.T[0][0])[i] = 0.f;
     (&sh.G[0][0])[i] = 0.f;
   }
-  panel_stage_in(S, n, k, 0, R, min(R, m), w, stage, NT);
+  panel_stage_in<R, NT>(S, n, k, 0, min(R, m), w, stage);
   __syncthreads();
   float a[CPW][RPL];
 #pragma unroll

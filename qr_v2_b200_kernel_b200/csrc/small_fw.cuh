@@ -94,7 +94,10 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
     float xm[RPL];
 #pragma unroll
     for (int i = 0; i < RPL; ++i) xm[i] = ((J32 && i > 0) || lane + 32 * i > j) ? a[jj][i] : 0.f;
-    float d[CPW], rowj[CPW];
+    // d[CPW] carries the squared norm of the tail scaled by 2^100 through the same butterfly,
+    // so the rare rescaled reflector needs no warp collective of its own (a shuffle inside a
+    // data-dependent branch costs the hot path a convergence barrier).
+    float d[CPW + 1], rowj[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
       float acc = 0.f;
@@ -107,26 +110,22 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
         for (int i = 1; i < RPL; ++i) t = (i == ij) ? a[c][i] : t;
       rowj[c] = t;
     }
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) rowj[c] = __shfl_sync(kFullMask, rowj[c], lj);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-      for (int c = 0; c < CPW; ++c) d[c] += __shfl_xor_sync(kFullMask, d[c], o);
-    Reflector rf;
-    if (reflector_needs_rescale(rowj[jj], d[jj])) {
+    {
       float su = 0.f;
 #pragma unroll
       for (int i = 0; i < RPL; ++i) {
         const float xu = xm[i] * kRescaleUp;
         su = fmaf(xu, xu, su);
       }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) su += __shfl_xor_sync(kFullMask, su, o);
-      rf = make_reflector_rescaled(rowj[jj], su);
-    } else {
-      rf = make_reflector_fast(rowj[jj], d[jj]);
+      d[CPW] = su;
     }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) rowj[c] = __shfl_sync(kFullMask, rowj[c], lj);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+      for (int c = 0; c <= CPW; ++c) d[c] += __shfl_xor_sync(kFullMask, d[c], o);
+    const Reflector rf = make_reflector_fast(rowj[jj], d[jj], d[CPW]);
     float z[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
