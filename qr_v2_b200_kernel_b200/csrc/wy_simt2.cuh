@@ -18,17 +18,6 @@
 
 namespace qrb200 {
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 constexpr int kV2Cols = 128, kV2Rows = 32, kV2Stages = 3;
 struct Vtc2Stage {
   float C[kV2Rows][kV2Cols];
@@ -526,7 +515,13 @@ __global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
   const int tid = threadIdx.x, c = tid & 31, g = tid >> 5;
   const int col = P.coff + blockIdx.x * 32 + c;
   const float* Tb = P.T + (long long)bidx * P.t_bstride;
-  for (int e = tid; e < 32 * 32; e += 256) Ts[e >> 5][e & 31] = Tb[e];
+  {
+    float tv[4];  // all four loads in flight before the stores
+#pragma unroll
+    for (int it = 0; it < 4; ++it) tv[it] = Tb[it * 256 + tid];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) Ts[(it * 256 + tid) >> 5][tid & 31] = tv[it];
+  }
   float wv[4] = {0.f, 0.f, 0.f, 0.f};
   if (col < nc) {
     // Splits in groups of four: sixteen independent loads in flight before the adds (which

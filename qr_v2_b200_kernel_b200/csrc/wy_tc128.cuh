@@ -209,18 +209,27 @@ struct TbuildParams {
   int ow;                 // outer block width (multiple of 32, <= 128)
 };
 // T's strictly lower part is zero, so it holds the Gram blocks the recurrence reads instead:
-// G[i][j] (block(i) < block(j)) lives at T[j][i]. 79 KB: two CTAs per SM.
+// G[i][j] (block(i) < block(j)) lives at T[j][i]; and each step's intermediate X sits in the
+// block column T[0:r, r:r+32] that the step then overwrites with its result. 66 KB: three CTAs
+// per SM.
 struct TbuildShared {
   float T[kOB][kOB + 1];
-  float X[96][33];
 };
 constexpr size_t kTbuildSmem = sizeof(TbuildShared);
 
-__global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
+__global__ void __launch_bounds__(256, 3) tbuild_kernel(TbuildParams P) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   TbuildShared& sh = *reinterpret_cast<TbuildShared*>(smem_raw);
   const int b = blockIdx.x, tid = threadIdx.x;
   const int ow = P.ow;
+  // The panel factors (diagonal blocks) land by cp.async while the Gram partials are summed.
+#pragma unroll
+  for (int it = 0; it < 16; ++it) {
+    const int e = it * 256 + tid;
+    const int blk = e >> 10, i = (e >> 5) & 31, j = e & 31;
+    if (32 * blk < ow) cp_async4(&sh.T[32 * blk + i][32 * blk + j], P.Tin + (long long)b * 4096 + e);
+  }
+  cp_async_commit();
   // Sum the Gram partials: 16 float4 per thread, all loads of a split issued together.
   {
     float4 g[16];
@@ -242,11 +251,7 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
       }
     }
   }
-  __syncthreads();
-  for (int e = tid; e < 4 * 32 * 32; e += 256) {
-    const int blk = e / 1024, i = (e / 32) % 32, j = e % 32;
-    if (32 * blk < ow) sh.T[32 * blk + i][32 * blk + j] = P.Tin[(long long)b * 4096 + e];
-  }
+  cp_async_wait<0>();
   __syncthreads();
   // Register-tiled block steps: thread (ti, tj) owns rows ti + 8 q (q < r/8... up to 12) of
   // column tj of the new 32-column block, so every shared load feeds several independent
@@ -255,7 +260,7 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
   for (int bb = 1; bb * 32 < ow; ++bb) {
     const int r = 32 * bb;  // rows of the new column block
     const int nq = r / 8;   // rows per thread: 4, 8 or 12
-    // X = G[0:r, r:r+32] T_bb     (T_bb upper triangular: c <= tj)
+    // X = G[0:r, r:r+32] T_bb     (T_bb upper triangular: c <= tj), into T[0:r, r:r+32]
     {
       float acc[12];
 #pragma unroll
@@ -268,7 +273,7 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
       }
 #pragma unroll
       for (int q = 0; q < 12; ++q)
-        if (q < nq) sh.X[ti + 8 * q][tj] = acc[q];
+        if (q < nq) sh.T[ti + 8 * q][r + tj] = acc[q];
     }
     __syncthreads();
     // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r, 0:r] upper triangular: c >= row)
@@ -277,13 +282,14 @@ __global__ void __launch_bounds__(256) tbuild_kernel(TbuildParams P) {
 #pragma unroll
       for (int q = 0; q < 12; ++q) acc[q] = 0.f;
       for (int c = ti; c < r; ++c) {
-        const float x = sh.X[c][tj];
+        const float x = sh.T[c][r + tj];
 #pragma unroll
         for (int q = 0; q < 12; ++q) {
           const int i = ti + 8 * q;
           if (q < nq && c >= i) acc[q] = fmaf(sh.T[i][c], x, acc[q]);
         }
       }
+      __syncthreads();  // every thread is done reading X
 #pragma unroll
       for (int q = 0; q < 12; ++q)
         if (q < nq) sh.T[ti + 8 * q][r + tj] = -acc[q];

@@ -59,7 +59,11 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Ho = P.H + (long long)bidx * n * n;
 
-  // (1) stage V and C (8 threads per row, 16 bytes each).
+  // (1) stage V, C and T (8 threads per row, 16 bytes each); T's four loads per thread are
+  // issued first, so every load of the stage is in flight together.
+  float tv[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) tv[it] = P.T[(long long)bidx * P.t_bstride + it * 256 + tid];
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
@@ -77,7 +81,11 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
     *reinterpret_cast<float4*>(&sh.V[rr][c]) = v;
     *reinterpret_cast<float4*>(&sh.C[rr][c]) = x;
   }
-  for (int e = tid; e < 32 * 32; e += 256) sh.T[e >> 5][e & 31] = P.T[(long long)bidx * P.t_bstride + e];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = it * 256 + tid;
+    sh.T[e >> 5][e & 31] = tv[it];
+  }
   __syncthreads();
   // (2) partial W over the slab: thread (rq, ig, cg) sums rows rq, rq + 4, ... for a 4 x 4 block.
   {
