@@ -161,50 +161,59 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
     }
   }
   cp_async_wait<0>();
-  // Epilogue (as tc_gemm128_kernel): thread t owns tile row t; the C slice for the next 32
-  // columns is requested before the current one is processed.
-  const int r = row0 + tid;
-  const bool row_ok = r < m;
+  // Epilogue: warp w owns tile rows 32 w .. 32 w + 31 (its TMEM lanes). Each 32-column chunk of
+  // the product goes through a padded shared tile (the operand ring is free once the last MMA
+  // is done), so that global traffic runs along rows: lane l handles row 4 i + (l >> 3),
+  // columns 4 (l & 7) .. + 3, and one warp access covers four whole 128-byte rows instead of
+  // 32 partial ones. The next chunk's C is in flight while the current one is processed.
+  const int lane = tid & 31, lr = lane >> 3, lq = lane & 7;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
-  const long long roff = (long long)(k + r) * n + k + w;
-  float4 cv[8];
-  auto load_c = [&](int q) {
-    const int cbase = col0 + q * 32;
+  constexpr int kPad = 36;  // row stride of the staging tile (floats): conflict-free float4 rows
+  float* stg = reinterpret_cast<float*>(&sh.st[0]) + warp * (32 * kPad);
+  auto load_chunk = [&](int q, float4 (&cv)[8]) {
+    const int c = col0 + q * 32 + 4 * lq;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      cv[e] = (MODE == MODE_UPD && row_ok && cbase + 4 * e < ncols)
-                  ? *reinterpret_cast<const float4*>(Sb + roff + cbase + 4 * e)
+    for (int i = 0; i < 8; ++i) {
+      const int r = row0 + 32 * warp + 4 * i + lr;
+      cv[i] = (MODE == MODE_UPD && r < m && c < ncols)
+                  ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + c)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   };
-  if (MODE == MODE_UPD) load_c(0);
+  float4 cA[8], cB[8];
+  if (MODE == MODE_UPD) load_chunk(0, cA);
   {
     const int last = NK - 1;
     ok = mbar_wait(&sh.mbar[last % kPipeSlots], (uint32_t)((last / kPipeSlots) & 1)) && ok;
   }
   tc_fence_after();
-#pragma unroll 1
+  __syncthreads();  // every warp is past its ring reads (splits) before any staging write
+#pragma unroll
   for (int q = 0; q < 4; ++q) {
     float pv[32];
     tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + q * 32, pv);
-    float4 cur[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) cur[e] = cv[e];
-    if (MODE == MODE_UPD && q + 1 < 4) load_c(q + 1);
-    if (!ok || !row_ok) continue;
-    const int cbase = col0 + q * 32;
-    if (MODE == MODE_Y) {
-      float* yrow = P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + cbase;
+    for (int e = 0; e < 8; ++e)
+      *reinterpret_cast<float4*>(stg + lane * kPad + 4 * e) = make_float4(pv[4 * e], pv[4 * e + 1], pv[4 * e + 2], pv[4 * e + 3]);
+    __syncwarp();
+    float4 (&cur)[8] = (q & 1) ? cB : cA;
+    float4 (&nxt)[8] = (q & 1) ? cA : cB;
+    if (MODE == MODE_UPD && q + 1 < 4) load_chunk(q + 1, nxt);
+    const int c = col0 + q * 32 + 4 * lq;
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(yrow + e) = make_float4(pv[e], pv[e + 1], pv[e + 2], pv[e + 3]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (cbase + 4 * e < ncols)
-          *reinterpret_cast<float4*>(Ho + roff + cbase + 4 * e) =
-              make_float4(cur[e].x - pv[4 * e], cur[e].y - pv[4 * e + 1], cur[e].z - pv[4 * e + 2], cur[e].w - pv[4 * e + 3]);
+    for (int i = 0; i < 8; ++i) {
+      const int rl = 4 * i + lr, r = row0 + 32 * warp + rl;
+      const float4 p = *reinterpret_cast<const float4*>(stg + rl * kPad + 4 * lq);
+      if (!ok || r >= m || c >= ncols) continue;
+      if (MODE == MODE_Y) {
+        *reinterpret_cast<float4*>(P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + c) = p;
+      } else {
+        *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + c) =
+            make_float4(cur[i].x - p.x, cur[i].y - p.y, cur[i].z - p.z, cur[i].w - p.w);
       }
     }
+    __syncwarp();  // the staging rows are read before the next chunk overwrites them
   }
   tc_fence_before();
   __syncthreads();
@@ -355,8 +364,16 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
     ok = mbar_wait(&sh.mbar[last % SLOTS], (uint32_t)((last / SLOTS) & 1)) && ok;
   }
   tc_fence_after();
-  const int col = col0 + tid;
-  float* out = P.Wp + (((long long)bidx * P.nsplit + split) * P.ncmax + col) * W;
+  __syncthreads();  // every warp is past its stage reads before any staging write
+  // Output row `col` (W floats) belongs to thread col - col0, i.e. to the TMEM lane of warp
+  // (col - col0) / 32. Each 32-float chunk of a warp's 32 rows goes through a padded shared
+  // tile so that lane l stores row 4 i + (l >> 3), floats 4 (l & 7) .. + 3: one warp store
+  // covers four whole 128-byte rows instead of 32 partial ones.
+  const int lr = lane >> 3, lq = lane & 7;
+  constexpr int kPad = 36;
+  float* stg = reinterpret_cast<float*>(&sh.st[0]) + warp * (32 * kPad);
+  const int ncol = GRAM ? W : nc;
+  float* outb = P.Wp + ((long long)bidx * P.nsplit + split) * P.ncmax * W;
 #pragma unroll 1
   for (int q = 0; q < W / 32; ++q) {
     float wv[32];
@@ -365,11 +382,18 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) wv[i] = 0.f;
     }
-    if (col < (GRAM ? W : nc)) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(out + q * 32 + i) = make_float4(wv[i], wv[i + 1], wv[i + 2], wv[i + 3]);
+    for (int e = 0; e < 8; ++e)
+      *reinterpret_cast<float4*>(stg + lane * kPad + 4 * e) = make_float4(wv[4 * e], wv[4 * e + 1], wv[4 * e + 2], wv[4 * e + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rl = 4 * i + lr, col = col0 + 32 * warp + rl;
+      if (col < ncol)
+        *reinterpret_cast<float4*>(outb + (long long)col * W + q * 32 + 4 * lq) =
+            *reinterpret_cast<const float4*>(stg + rl * kPad + 4 * lq);
     }
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
