@@ -742,6 +742,32 @@ static int num_sms() {
 // FP32 compact-WY update of columns [k + w + coff, cend) by the panel at k (the narrow update
 // inside an outer block, or either half of a single-level look-ahead update). T factors sit
 // t_bstride elements apart.
+// Resident CTAs per SM of the wide FP32 update kernel wy_upd4 (QRB200_UPD_PERSIST; default 0:
+// one CTA per tile). A persistent grid (2 per SM) that fills every SM before the next
+// high-priority panel launches keeps that panel waiting until the whole update is done, which
+// made C4 / C5 times bimodal (C4 5.2 or 5.9 ms from one process to the next); one-tile CTAs
+// free SMs continuously and the look-ahead chain's kernels go first.
+static int upd_persist() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_UPD_PERSIST");
+    v = e ? atoi(e) : 0;
+    if (v < 0 || v > 8) v = 0;
+  }
+  return v;
+}
+
+// The wide 32-column V^T C of the single-level schedule on tcgen05 (3xTF32, partials stored
+// transposed, then wy_tw2t; default), or QRB200_U2_TC=0 for the FP32 wy_vtc3 kernel.
+static bool u2_tc() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("QRB200_U2_TC");
+    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static cudaError_t launch_wy(const float* src, long long sbs, float* H, const float* T, long long t_bstride,
                              const Workspace& ws, long long batch, int n, int k, int w, int coff, int cend,
                              cudaStream_t s, bool allow_u1 = false) {
@@ -806,7 +832,22 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(256), kU1Smem, s,
                     (unsigned)cp, true, wp);
   }
-  if (vec) {
+  const bool vtc_tc = vec && u2_tc() && ncl > kV2Cols && wy3_enabled();
+  if (vtc_tc) {
+    static PerDevice configured_tc;
+    const int dev = current_device();
+    if (!configured_tc.done(dev)) {
+      cudaError_t e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<32, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)vtcw_pipe_smem<32, false, 3>());
+      if (e != cudaSuccess) return e;
+      configured_tc.mark(dev);
+    }
+  }
+  if (vtc_tc) {
+    LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
+    tc_vtcw_pipe_kernel<32, false, 3><<<dim3(cdiv(ncl, kTcCols), wp.nsplit, (unsigned)batch), 128,
+                                         vtcw_pipe_smem<32, false, 3>(), s>>>(wp);
+  } else if (vec) {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
     if (ncl > kV2Cols && wy3_enabled())
     {
@@ -830,7 +871,9 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   }
   {
     LaunchScope ls(K_TW, (double)batch * w * w * ncl, 4.0 * batch * (wp.nsplit + 1.0) * w * ncl);
-    if (vec)
+    if (vtc_tc)
+      ep = launch_k(wy_tw2t_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp);
+    else if (vec)
       ep = launch_k(wy_tw2_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp);
     else
       wy_tw_kernel<kNB><<<dim3(cdiv(ncl, 128), (unsigned)batch), 128, 0, s>>>(wp);
@@ -840,7 +883,8 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     if (vec && wy3_enabled() && wy4_enabled() && ncl > kU3Cols) {
       const int tc = cdiv(ncl, kU4Cols), tr = cdiv(m, kU4Rows);
       const long long nt = (long long)tc * tr * batch;
-      const int grid = (int)std::min<long long>(nt, 2LL * num_sms());
+      const int pers = upd_persist();
+      const int grid = (int)(pers > 0 ? std::min<long long>(nt, (long long)pers * num_sms()) : nt);
       ep = launch_k(wy_upd4_kernel, dim3(grid), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt);
     } else if (vec && wy3_enabled()) {
       if (ncl <= 32 && narrow_tiles()) {

@@ -400,4 +400,63 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
   if (warp == 0) tmem_dealloc(tmem, W);
 }
 
+// ---------------------------------------------------------------------------------------
+// W2 = T^T sum_s Wp[s] for partials stored transposed (Wp[s][col][0..32), as
+// tc_vtcw_pipe_kernel<32, ...> writes them): 32 columns per CTA. Thread (column tid >> 3, row
+// quad tid & 7) adds its float4 of every split (eight lanes read one whole 128-byte row), in
+// split order; then the T^T product as wy_tw2_kernel.
+__global__ void __launch_bounds__(256) wy_tw2t_kernel(WyParams P) {
+  griddep_launch_wait();
+  __shared__ float Ts[32][33];
+  __shared__ float Ws[32][33];
+  const int bidx = blockIdx.y;
+  const int nc = P.cend - P.k - P.w;
+  const int tid = threadIdx.x;
+  const float* Tb = P.T + (long long)bidx * P.t_bstride;
+  float tv[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) tv[it] = Tb[it * 256 + tid];
+  {
+    const int cl = tid >> 3, g = tid & 7;
+    const int col = P.coff + blockIdx.x * 32 + cl;
+    float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col < nc) {
+      const float* W0 = P.Wp + ((long long)bidx * P.nsplit * P.ncmax + col) * 32 + 4 * g;
+      const long long sstride = 32LL * P.ncmax;
+      int s = 0;
+      for (; s + 4 <= P.nsplit; s += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const float4*>(W0 + (s + u) * sstride);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          wv.x += x[u].x; wv.y += x[u].y; wv.z += x[u].z; wv.w += x[u].w;
+        }
+      }
+      for (; s < P.nsplit; ++s) {
+        const float4 x = *reinterpret_cast<const float4*>(W0 + s * sstride);
+        wv.x += x.x; wv.y += x.y; wv.z += x.z; wv.w += x.w;
+      }
+    }
+    Ws[4 * g + 0][cl] = wv.x;
+    Ws[4 * g + 1][cl] = wv.y;
+    Ws[4 * g + 2][cl] = wv.z;
+    Ws[4 * g + 3][cl] = wv.w;
+  }
+#pragma unroll
+  for (int it = 0; it < 4; ++it) Ts[(it * 256 + tid) >> 5][tid & 31] = tv[it];
+  __syncthreads();
+  const int c = tid & 31, g = tid >> 5;
+  const int col = P.coff + blockIdx.x * 32 + c;
+  if (col >= nc) return;
+  float* out = P.W2 + (long long)bidx * 32 * P.ncmax;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int i = 4 * g + a;
+    float acc = 0.f;
+    for (int cc = 0; cc <= i; ++cc) acc = fmaf(Ts[cc][i], Ws[cc][c], acc);
+    out[(long long)i * P.ncmax + col] = acc;
+  }
+}
+
 }  // namespace qrb200
