@@ -225,9 +225,20 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
 // with the rows streamed by cp.async straight into the SW128_32B operand layout and split in
 // place (V masked to its unit lower trapezoid in the panel's first 128 rows). Same tiles and
 // arithmetic, so results agree bit for bit.
+// One K stage of the pipelined V^T C / Gram kernel: V first, then C (the Gram reads V as both
+// operands, so its C buffers shrink to a placeholder: 18 KB per stage instead of 32, four CTAs
+// per SM). Every buffer starts on a 1 KB boundary.
+template <int W, bool GRAM>
+struct VtcwPipeStage {
+  float v_hi[kWChunk * W];
+  float v_lo[kWChunk * W];
+  float c_hi[GRAM ? 256 : kWChunk * kTcCols];
+  float c_lo[GRAM ? 256 : kWChunk * kTcCols];
+};
+
 template <int W, bool GRAM, int SLOTS>
 struct VtcwPipeShared {
-  VtcwStage<W> st[SLOTS];
+  VtcwPipeStage<W, GRAM> st[SLOTS];
   uint64_t mbar[SLOTS];
   uint32_t tmem;
 };
@@ -277,7 +288,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
     kk = (atom >> 2) * 4 + kr;
   };
   auto issue = [&](int ch) {
-    VtcwStage<W>& st = sh.st[ch % SLOTS];
+    VtcwPipeStage<W, GRAM>& st = sh.st[ch % SLOTS];
     const int r0 = r_begin + ch * kWChunk;
 #pragma unroll
     for (int it = 0; it < NV; ++it) {
@@ -317,7 +328,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
     }
     cp_async_commit();
     cp_async_wait<kAhead>();
-    VtcwStage<W>& st = sh.st[ch % SLOTS];
+    VtcwPipeStage<W, GRAM>& st = sh.st[ch % SLOTS];
     const int r0 = r_begin + ch * kWChunk;
 #pragma unroll
     for (int it = 0; it < NV; ++it) {
