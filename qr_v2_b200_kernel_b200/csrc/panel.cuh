@@ -370,7 +370,7 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
 // Two CTAs per SM for the 8-warp shape (<= 128 registers), so one CTA's reflector latency
 // overlaps another matrix's panel.
 template <int RPL, int CPW, bool HAS_T>
-__global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 8 ? 3 : 2) : 1)) panel_owner_kernel(PanelParams P) {
+__global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 12 ? 3 : 2) : 1)) panel_owner_kernel(PanelParams P) {
   constexpr int NW = 32 / CPW;
   __shared__ OwnerShared<RPL, CPW> sh;
   const int bidx = blockIdx.y;

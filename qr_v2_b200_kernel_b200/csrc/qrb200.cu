@@ -505,6 +505,7 @@ static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batc
   }
   if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
   if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
+  if (m <= 384) return launch_owner_cpw<12>(q, batch, s);  // three CTAs per SM (two at 16 rows a lane)
   if (m <= 512) return launch_owner_cpw<16>(q, batch, s);
   if (m <= 1024 && panel_lookahead()) return launch_la<32, 2>(q, batch, s);
   if (m <= 1024) return launch_panel<16, true>(q, cdiv(m, 512), batch, s);
