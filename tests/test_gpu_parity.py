@@ -111,14 +111,15 @@ def test_edge_matrices():
     assert (tau == 0).all() and (H == 0).all()
 
 
-@pytest.mark.parametrize("n", [96, 200, 600])
+@pytest.mark.parametrize("n", [96, 200, 600, 1536])
 def test_tiny_scale_keeps_q_orthogonal(n):
     """Entries near 1e-20 square into fp32's subnormal range (fewer than 24 bits), which left
     tau inconsistent with its vector on short column tails; the rescaled reflector keeps Q
     orthogonal. n = 96: whole-matrix kernel; 200: owner panels; 600: cluster panels (tails of
-    513+ rows, whose sums stay accurate at 1e-20) and factor-warp panels. Much smaller entries
-    are out of range: the panels form tail-by-column dot products before normalising the tail
-    (as the reference panel does), and below about 1e-22 those products underflow."""
+    513+ rows, whose sums stay accurate at 1e-20) and owner panels; 1536: cluster and
+    factor-warp panels. Much smaller entries are out of range: the panels form tail-by-column
+    dot products before normalising the tail (as the reference panel does), and below about
+    1e-22 those products underflow."""
     g = torch.Generator().manual_seed(n)
     A = (torch.randn(3, n, n, generator=g) * 1e-20).cuda()
     H, tau = _run(A)
