@@ -794,6 +794,9 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   wp.coff = coff;
   const double bm = (double)batch * m;
   cudaError_t ep = cudaSuccess;  // first launch error of the three kernels
+  auto note = [&ep](cudaError_t e) {
+    if (ep == cudaSuccess) ep = e;
+  };
   const bool vec = wy2_enabled() && w == kNB && (n % 4) == 0 && (sbs % 4) == 0 &&
                    ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(H)) & 15u) == 0;
   if (vec) {
@@ -857,16 +860,16 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       if (wy_vtc8x8())
         wy_vtc4_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 128, kVtc3Smem, s>>>(wp);
       else
-        ep = launch_k(wy_vtc3_kernel, dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc3Smem, s, 0, true, wp);
+        note(launch_k(wy_vtc3_kernel, dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc3Smem, s, 0, true, wp));
     }
     else
     {
       if (ncl <= 32 && narrow_tiles())
-        ep = launch_k(wy_vtcn_kernel<32>, dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<32>(), s, 0, true, wp);
+        note(launch_k(wy_vtcn_kernel<32>, dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<32>(), s, 0, true, wp));
       else if (ncl <= 64 && narrow_tiles())
-        ep = launch_k(wy_vtcn_kernel<64>, dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<64>(), s, 0, true, wp);
+        note(launch_k(wy_vtcn_kernel<64>, dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<64>(), s, 0, true, wp));
       else
-        ep = launch_k(wy_vtc2_kernel, dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc2Smem, s, 0, true, wp);
+        note(launch_k(wy_vtc2_kernel, dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc2Smem, s, 0, true, wp));
     }
   } else {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
@@ -875,9 +878,9 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   {
     LaunchScope ls(K_TW, (double)batch * w * w * ncl, 4.0 * batch * (wp.nsplit + 1.0) * w * ncl);
     if (vtc_tc)
-      ep = launch_k(wy_tw2t_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp);
+      note(launch_k(wy_tw2t_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp));
     else if (vec)
-      ep = launch_k(wy_tw2_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp);
+      note(launch_k(wy_tw2_kernel, dim3(cdiv(ncl, 32), (unsigned)batch), dim3(256), 0, s, 0, true, wp));
     else
       wy_tw_kernel<kNB><<<dim3(cdiv(ncl, 128), (unsigned)batch), 128, 0, s>>>(wp);
   }
@@ -888,18 +891,18 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       const long long nt = (long long)tc * tr * batch;
       const int pers = upd_persist();
       const int grid = (int)(pers > 0 ? std::min<long long>(nt, (long long)pers * num_sms()) : nt);
-      ep = launch_k(wy_upd4_kernel, dim3(grid), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt);
+      note(launch_k(wy_upd4_kernel, dim3(grid), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt));
     } else if (vec && wy3_enabled()) {
       if (ncl <= 32 && narrow_tiles()) {
         const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
         const long long nt = (long long)tc * tr * batch;
         const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        ep = launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt);
+        note(launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt));
       } else {
         const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
         const long long nt = (long long)tc * tr * batch;
         const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        ep = launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt);
+        note(launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt));
       }
     } else if (vec)
       wy_upd2_kernel<<<dim3(cdiv(ncl, kU2Cols), cdiv(m, kU2Rows), (unsigned)batch), 256, 0, s>>>(wp);
