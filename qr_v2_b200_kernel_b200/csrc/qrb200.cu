@@ -912,19 +912,47 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   return ep != cudaSuccess ? ep : cudaGetLastError();
 }
 
-// Look-ahead streams of one device: the critical chain (panels, narrow updates, T, Y and the
-// update of the next outer block's columns) runs on a high-priority stream, the rest of each
-// wide update on a low-priority one, forked from and joined back into the caller's stream.
+// Look-ahead streams: the critical chain (panels, narrow updates, T, Y and the update of the
+// next outer block's columns) runs on a high-priority stream, the rest of each wide update on a
+// low-priority one, forked from and joined back into the caller's stream.
 struct LookaheadStreams {
   cudaStream_t p = nullptr, u = nullptr;
   cudaEvent_t fork = nullptr, y = nullptr, u2 = nullptr, pj = nullptr, uj = nullptr;
 };
 constexpr int kMaxDevices = 64;
-static std::mutex g_la_mu[kMaxDevices];  // one two-level enqueue per device at a time
-static LookaheadStreams g_la[kMaxDevices];
 
-static cudaError_t lookahead_streams(int dev, LookaheadStreams** out) {
-  LookaheadStreams& L = g_la[dev];
+// One set of look-ahead streams per caller stream (up to kLaSlots per device), so calls enqueued
+// on different streams -- the host API's batch pieces, or several host threads -- factor
+// concurrently instead of queueing behind one shared pair. Calls on one caller stream reuse its
+// set and stay ordered; its mutex keeps one enqueue at a time on a set. Beyond kLaSlots caller
+// streams, sets are shared (and those calls serialised), which stays correct.
+constexpr int kLaSlots = 8;
+struct LaSlot {
+  std::mutex mu;
+  bool used = false;
+  cudaStream_t owner = nullptr;
+  LookaheadStreams L;
+};
+static std::mutex g_la_table_mu[kMaxDevices];
+static LaSlot g_la_slots[kMaxDevices][kLaSlots];
+
+static LaSlot& la_slot(int dev, cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(g_la_table_mu[dev]);
+  LaSlot* free_slot = nullptr;
+  for (LaSlot& sl : g_la_slots[dev]) {
+    if (sl.used && sl.owner == s) return sl;
+    if (!sl.used && free_slot == nullptr) free_slot = &sl;
+  }
+  if (free_slot != nullptr) {
+    free_slot->used = true;
+    free_slot->owner = s;
+    return *free_slot;
+  }
+  return g_la_slots[dev][(reinterpret_cast<uintptr_t>(s) >> 4) % kLaSlots];
+}
+
+static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
+  LookaheadStreams& L = slot.L;
   if (!L.p) {
     int least = 0, greatest = 0;
     cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
@@ -1124,9 +1152,10 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
   // when no outer block has columns beyond the next one (n <= 256).
   if (t_prof || !lookahead_enabled() || n <= 2 * kOB || dev >= kMaxDevices)
     return two_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
-  std::lock_guard<std::mutex> lk(g_la_mu[dev]);
+  LaSlot& slot = la_slot(dev, s);
+  std::lock_guard<std::mutex> lk(slot.mu);
   LookaheadStreams* L = nullptr;
-  if ((e = lookahead_streams(dev, &L)) != cudaSuccess) return e;
+  if ((e = lookahead_streams(slot, &L)) != cudaSuccess) return e;
   if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
@@ -1185,14 +1214,15 @@ static cudaError_t single_level_body(const float* A, float* H, float* tau, long 
   return cudaSuccess;
 }
 
-// Shared fork/join around a look-ahead body: the body runs on the device's two look-ahead
-// streams, both joined back into the caller's stream (also after a failed launch).
+// Shared fork/join around a look-ahead body: the body runs on the caller stream's two
+// look-ahead streams, both joined back into the caller's stream (also after a failed launch).
 template <class Body>
 static cudaError_t with_lookahead(int dev, cudaStream_t s, Body body) {
-  std::lock_guard<std::mutex> lk(g_la_mu[dev]);
+  LaSlot& slot = la_slot(dev, s);
+  std::lock_guard<std::mutex> lk(slot.mu);
   LookaheadStreams* L = nullptr;
   cudaError_t e;
-  if ((e = lookahead_streams(dev, &L)) != cudaSuccess) return e;
+  if ((e = lookahead_streams(slot, &L)) != cudaSuccess) return e;
   if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;

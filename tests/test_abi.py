@@ -105,6 +105,8 @@ def test_host_api_rejects_bad_inputs_on_cpu():
         custom_kernel_host(torch.zeros(2, 3, 4))
     with pytest.raises(TypeError):
         custom_kernel_host(torch.zeros(2, 3, 3, dtype=torch.float64))
-    # pieces: one below 64 matrices, otherwise at least 32 matrices each, at most four
-    assert _host_chunks(8) == 1 and _host_chunks(63) == 1
-    assert _host_chunks(64) == 2 and _host_chunks(640) == 4
+    # pieces by input size: one below 32 MB, two below 192 MB, else four; at most one per matrix
+    assert _host_chunks(8, 128) == 1  # C1: 0.5 MB
+    assert _host_chunks(8, 2048) == 2 and _host_chunks(2, 4096) == 2  # C4, C5: 134 MB
+    assert _host_chunks(64, 1024) == 4 and _host_chunks(640, 512) == 4  # C3, C2
+    assert _host_chunks(1, 4096) == 1  # never more pieces than matrices
