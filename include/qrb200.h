@@ -20,7 +20,12 @@
  * Two calls that share a workspace must be ordered on the same stream.
  *
  * Every entry point returns a status (QRB200_OK = 0). Device-side failures found by a
- * bounded wait are reported by qrb200_device_status() after the stream has completed.
+ * bounded wait are reported by qrb200_last_status() (no synchronisation) or
+ * qrb200_device_status() once the work has executed.
+ *
+ * The first call on each device registers that device's failure word with a synchronous
+ * symbol copy: make it before any stream capture on that device. The library does not
+ * survive a cudaDeviceReset (its per-device set-up is not redone).
  */
 #ifndef QRB200_H_
 #define QRB200_H_
@@ -55,16 +60,55 @@ int qrb200_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_
                      int64_t a_batch_stride, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* ---- using the factorisation: Q and Q^T (the reference's checker step, sorgqr/sormqr) ---- */
+
+/* Bytes of scratch that qrb200_ormqr_f32 (nrhs columns) and qrb200_orgqr_f32 (nrhs = n) need. */
+size_t qrb200_apply_workspace_bytes(int64_t batch, int64_t n, int64_t nrhs);
+
+/* C <- Q^T C (transpose != 0) or Q C (transpose == 0), in place, for each matrix of the batch:
+ * Q = H_0 H_1 ... H_{n-1} of (H, tau) in the layout qrb200_geqrf_f32 writes (H batch x n x n,
+ * tau batch x n, contiguous), C batch x n x nrhs row-major contiguous. Left side only, as
+ * torch.ormqr(H, tau, C, left=True, transpose=...). Blocked compact-WY on the tensor cores
+ * (3xTF32). Needs n % 4 == 0, nrhs % 4 == 0, 1 <= n <= 4096, H and C 16-byte aligned
+ * (QRB200_ERR_ARG otherwise). Replaces the LAPACK/cuSOLVER sormqr that a consumer of the
+ * reference's (H, tau) output would call (README.md:42-50 of the reference: Q is implicit). */
+int qrb200_ormqr_f32(const float* H, const float* tau, float* C, int64_t batch, int64_t n, int64_t nrhs,
+                     int transpose, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Q (batch x n x n, row-major contiguous, written) = householder_product(H, tau) for square H:
+ * replaces torch.linalg.householder_product, which the reference's checker calls on every
+ * output (harness/reference.py:206). Same requirements as qrb200_ormqr_f32 (nrhs = n). */
+int qrb200_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int64_t n, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* qrb200_status_string(int status);
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int qrb200_version(void);
 
-/* Device-side error word of the current device (0 = none), cleared by the read.
- * Uses a synchronous symbol copy (it waits for prior work on the legacy default stream);
- * call it after the stream that ran the QR has completed. */
+/* Device-side failures. Every wait inside a kernel is bounded; a kernel whose wait expires
+ * records the failure, skips its outputs and returns (the results of that call are invalid).
+ * The record lands in a device word and in a mapped pinned host word per device.
+ *
+ * qrb200_last_status: QRB200_ERR_TIMEOUT if a kernel on the current device has recorded a
+ * failure since the last read, else QRB200_OK; the host word is cleared by the read. It makes
+ * no CUDA call beyond cudaGetDevice and never waits, so it sees failures of work that has
+ * already executed (read it after synchronising, or before the next call as the Python operator
+ * does). *site_out (may be NULL) receives the wait site: 1 tensor-core mbarrier, 2 whole-matrix
+ * hand-off, 3 cluster-panel exchange, 4 self-test. No counterpart in the reference (its only
+ * failure mechanism is the exception fallback of submission.py:572-596). */
+int qrb200_last_status(int* site_out);
+
+/* Synchronous variant: reads (and clears) the device word of the current device with a symbol
+ * copy (which waits for prior work on the legacy default stream) and clears the host word;
+ * *status_out = QRB200_ERR_TIMEOUT or QRB200_OK. */
 int qrb200_device_status(int* status_out);
+
+/* Test hook: one warp waits `polls` times on a barrier that nothing completes, so the wait runs
+ * out and reports site 4 through the same path as the factorisation kernels. Asynchronous on
+ * `stream`; leaves the device usable. */
+int qrb200_selftest_wait_timeout(uint32_t polls, void* stream);
 
 /* ---- allocation-free entry (no counterpart in the reference) ------------------------- */
 
@@ -95,6 +139,15 @@ int qrb200_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch
                              int64_t a_batch_stride, void* stream);
 
 /* ---- diagnostics (no counterpart in the reference; used by bench.py) ---------------- */
+
+/* The two 3xTF32 tcgen05 GEMMs of the 128-wide trailing update on their own, for accuracy
+ * tests: for each matrix of H (batch x n x n, contiguous, 129 <= n <= 1024, n % 4 == 0),
+ * V = the unit lower trapezoid of H[:, 0:128] (entries above the diagonal of that block read as
+ * zero, the diagonal as one), C = H[:, 128:n]; computes C <- C - Y (V^T C) with Y given
+ * (batch x n x 128, row-major), through W^T = C^T V (tc_vtc128) and C -= Y W (tc_upd128). The
+ * first 128 columns of H are left as they are. Workspace as for qrb200_geqrf_f32(batch, n). */
+int qrb200_diag_wide_update_f32(float* H, const float* Y, int64_t batch, int64_t n, void* workspace,
+                                size_t workspace_bytes, void* stream);
 
 /* Number of kernels this library has launched in the process so far (all threads). */
 long long qrb200_launch_count(void);

@@ -37,10 +37,20 @@ SIGNATURES = {
     "qrb200_geqrf_f32_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                 ctypes.c_void_p]),
+    "qrb200_apply_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+    "qrb200_ormqr_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_size_t, ctypes.c_void_p]),
+    "qrb200_orgqr_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "qrb200_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "qrb200_version": (ctypes.c_int, []),
     "qrb200_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "qrb200_last_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
+    "qrb200_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
     "qrb200_launch_count": (ctypes.c_longlong, []),
+    "qrb200_diag_wide_update_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                                   ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "qrb200_profile_geqrf_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
@@ -85,3 +95,17 @@ def load(path: str | None = None) -> ctypes.CDLL:
 def check(status: int, what: str) -> None:
     if status != QRB200_OK:
         raise QRB200Error(status, what)
+
+
+def check_last_status(what: str = "an earlier call") -> None:
+    """Raise :class:`QRB200Error` (QRB200_ERR_TIMEOUT) if a kernel on the current device has
+    recorded an expired wait since the last check (the results of that call are invalid).
+
+    Reads the library's mapped host word: no CUDA synchronisation, so it reports failures of
+    work that has already executed on the device. The word is cleared by the read.
+    """
+    site = ctypes.c_int(0)
+    st = load().qrb200_last_status(ctypes.byref(site))
+    if st == QRB200_ERR_TIMEOUT:
+        raise QRB200Error(st, f"{what} (device wait site {site.value})")
+    check(st, "last_status")

@@ -11,7 +11,9 @@ as the harness calls it (``harness/eval.py:189-211``):
   synchronisation, so CUDA events recorded around the call on that stream time it
   (``harness/eval.py:205-210``);
 * errors raise: ``TypeError``/``ValueError`` for a wrong argument, ``RuntimeError`` for a
-  non-CUDA input (there is no CPU path) and :class:`QRB200Error` for a failing C-ABI call.
+  non-CUDA input (there is no CPU path) and :class:`QRB200Error` for a failing C-ABI call or
+  for a device-side wait that expired in an earlier call on the same device (checked at the
+  start of every call from a mapped host word, without synchronising).
   The reference instead falls back to ``torch.geqrf`` (``submission.py:572-596``); this
   operator never falls back.
 
@@ -28,10 +30,9 @@ import torch
 
 from . import _lib
 
-__all__ = ["custom_kernel", "custom_kernel_host", "geqrf", "workspace_bytes"]
+__all__ = ["custom_kernel", "custom_kernel_host", "geqrf", "workspace_bytes", "householder_product", "ormqr"]
 
 _ws_lock = threading.Lock()
-_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def workspace_bytes(batch: int, n: int) -> int:
@@ -39,33 +40,61 @@ def workspace_bytes(batch: int, n: int) -> int:
     return int(_lib.load().qrb200_workspace_bytes(int(batch), int(n)))
 
 
-def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
-    """Callee-owned scratch, cached per (device, stream) and grown on demand.
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Callee-owned scratch for one call, from the torch caching allocator on the current stream.
 
-    Calls on one stream are ordered, so they may share it; another stream gets its own.
+    The tensor is released when the call returns (after the work is enqueued); the allocator
+    hands its block only to later work on the same stream, or to another stream once this
+    stream's work is done, so scratch is never shared by unordered calls. After the first call
+    of a shape this is a cache hit, not a device allocation.
     """
     if nbytes == 0:
         return None
-    key = (device.index, stream)
-    with _ws_lock:
-        buf = _ws_cache.get(key)
-        if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            _ws_cache[key] = buf
-        return buf
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _check_operands(A: torch.Tensor, H: torch.Tensor, tau: torch.Tensor) -> tuple[int, int, int]:
+    """Validate :func:`geqrf`'s operands before any pointer reaches the C ABI."""
+    for name, t in (("A", A), ("H", H), ("tau", tau)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.dtype != torch.float32:
+            raise TypeError(f"{name} must be torch.float32, got {t.dtype}")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor (qrb200 has no CPU path)")
+        if t.device != A.device:
+            raise ValueError(f"{name} is on {t.device}, A on {A.device}")
+    if A.dim() != 3 or A.shape[-1] != A.shape[-2]:
+        raise ValueError(f"A must be (batch, n, n), got {tuple(A.shape)}")
+    batch, n = int(A.shape[0]), int(A.shape[-1])
+    if tuple(H.shape) != (batch, n, n) or not H.is_contiguous():
+        raise ValueError(f"H must be a contiguous ({batch}, {n}, {n}) tensor, got {tuple(H.shape)}")
+    if tuple(tau.shape) != (batch, n) or not tau.is_contiguous():
+        raise ValueError(f"tau must be a contiguous ({batch}, {n}) tensor, got {tuple(tau.shape)}")
+    if batch > 0 and n > 0 and (A.stride(-1) != 1 or A.stride(-2) != n or (batch > 1 and A.stride(0) < n * n)):
+        raise ValueError("A must have unit column stride, row stride n and batch stride >= n*n")
+    abs_ = int(A.stride(0)) if batch > 1 else n * n
+    return batch, n, abs_
 
 
 def geqrf(A: torch.Tensor, H: torch.Tensor, tau: torch.Tensor) -> None:
-    """Factor ``A`` into caller-provided ``H`` and ``tau`` (same device, contiguous float32)."""
+    """Factor ``A`` into caller-provided ``H`` and ``tau``.
+
+    ``A``: (batch, n, n) float32 CUDA, rows contiguous (unit column stride, row stride n, any
+    batch stride >= n*n); ``H`` (batch, n, n) and ``tau`` (batch, n): contiguous float32 on A's
+    device. Raises ``TypeError``/``ValueError``/``RuntimeError`` for bad operands before
+    anything is launched, :class:`QRB200Error` for a failing C-ABI call or a device-side wait
+    that expired in an earlier call on this device.
+    """
+    batch, n, abs_ = _check_operands(A, H, tau)
     lib = _lib.load()
-    batch, n = int(A.shape[0]), int(A.shape[-1])
     if batch == 0 or n == 0:
         return
-    abs_ = int(A.stride(0)) if batch > 1 else n * n
     with torch.cuda.device(A.device):
+        _lib.check_last_status()
         stream = torch.cuda.current_stream(A.device).cuda_stream
         need = workspace_bytes(batch, n)
-        ws = _workspace(A.device, stream, need)
+        ws = _workspace(A.device, need)
         st = lib.qrb200_geqrf_f32(
             ctypes.c_void_p(A.data_ptr()), ctypes.c_void_p(H.data_ptr()), ctypes.c_void_p(tau.data_ptr()),
             batch, n, abs_,
@@ -93,6 +122,86 @@ def custom_kernel(data: torch.Tensor):
     tau = torch.empty((batch, n), dtype=torch.float32, device=A.device)
     geqrf(A, H, tau)
     return H, tau
+
+
+def _check_factors(H: torch.Tensor, tau: torch.Tensor) -> tuple[int, int]:
+    """(H, tau) as :func:`custom_kernel` returns them: contiguous float32 CUDA, n % 4 == 0."""
+    for name, t in (("H", H), ("tau", tau)):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.dtype != torch.float32:
+            raise TypeError(f"{name} must be torch.float32, got {t.dtype}")
+        if not t.is_cuda:
+            raise RuntimeError(f"{name} must be a CUDA tensor (qrb200 has no CPU path)")
+    if H.dim() != 3 or H.shape[-1] != H.shape[-2]:
+        raise ValueError(f"H must be (batch, n, n), got {tuple(H.shape)}")
+    batch, n = int(H.shape[0]), int(H.shape[-1])
+    if tuple(tau.shape) != (batch, n):
+        raise ValueError(f"tau must be ({batch}, {n}), got {tuple(tau.shape)}")
+    if tau.device != H.device:
+        raise ValueError(f"tau is on {tau.device}, H on {H.device}")
+    if n % 4 != 0:
+        raise ValueError("the tensor-core Q application needs n % 4 == 0")
+    return batch, n
+
+
+def householder_product(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
+    """``Q = H_0 H_1 ... H_{n-1}`` of square factors: ``torch.linalg.householder_product(H, tau)``
+    on the B200 (the reference's checker step, ``harness/reference.py:206``).
+
+    ``H`` (batch, n, n) and ``tau`` (batch, n) float32 CUDA as :func:`custom_kernel` returns
+    them; n % 4 == 0. Returns a fresh (batch, n, n) tensor; enqueued on the current stream.
+    """
+    batch, n = _check_factors(H, tau)
+    Q = torch.empty((batch, n, n), dtype=torch.float32, device=H.device)
+    if batch == 0 or n == 0:
+        return Q
+    H, tau = H.contiguous(), tau.contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(H.device):
+        _lib.check_last_status()
+        stream = torch.cuda.current_stream(H.device).cuda_stream
+        need = int(lib.qrb200_apply_workspace_bytes(batch, n, n))
+        ws = _workspace(H.device, need)
+        st = lib.qrb200_orgqr_f32(ctypes.c_void_p(H.data_ptr()), ctypes.c_void_p(tau.data_ptr()),
+                                  ctypes.c_void_p(Q.data_ptr()), batch, n, ctypes.c_void_p(ws.data_ptr()), need,
+                                  ctypes.c_void_p(stream))
+    _lib.check(st, "orgqr_f32")
+    return Q
+
+
+def ormqr(H: torch.Tensor, tau: torch.Tensor, C: torch.Tensor, transpose: bool = False) -> torch.Tensor:
+    """``Q^T C`` (``transpose=True``) or ``Q C`` for ``Q`` of the factors ``(H, tau)``:
+    ``torch.ormqr(H, tau, C, left=True, transpose=transpose)`` on the B200.
+
+    ``C``: (batch, n, nrhs) float32 on H's device, nrhs % 4 == 0. Returns a new tensor (C is not
+    modified); enqueued on the current stream. Least squares: ``R x = (Q^T b)[:n]``.
+    """
+    batch, n = _check_factors(H, tau)
+    if not isinstance(C, torch.Tensor) or C.dtype != torch.float32:
+        raise TypeError("C must be a float32 torch.Tensor")
+    if C.device != H.device:
+        raise ValueError(f"C is on {C.device}, H on {H.device}")
+    if C.dim() != 3 or int(C.shape[0]) != batch or int(C.shape[1]) != n:
+        raise ValueError(f"C must be ({batch}, {n}, nrhs), got {tuple(C.shape)}")
+    nrhs = int(C.shape[2])
+    if nrhs % 4 != 0:
+        raise ValueError("the tensor-core Q application needs nrhs % 4 == 0")
+    out = C.contiguous().clone()
+    if batch == 0 or n == 0 or nrhs == 0:
+        return out
+    H, tau = H.contiguous(), tau.contiguous()
+    lib = _lib.load()
+    with torch.cuda.device(H.device):
+        _lib.check_last_status()
+        stream = torch.cuda.current_stream(H.device).cuda_stream
+        need = int(lib.qrb200_apply_workspace_bytes(batch, n, nrhs))
+        ws = _workspace(H.device, need)
+        st = lib.qrb200_ormqr_f32(ctypes.c_void_p(H.data_ptr()), ctypes.c_void_p(tau.data_ptr()),
+                                  ctypes.c_void_p(out.data_ptr()), batch, n, nrhs, 1 if transpose else 0,
+                                  ctypes.c_void_p(ws.data_ptr()), need, ctypes.c_void_p(stream))
+    _lib.check(st, "ormqr_f32")
+    return out
 
 
 _chunk_streams: dict[int, list] = {}

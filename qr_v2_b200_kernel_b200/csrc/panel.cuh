@@ -1,40 +1,18 @@
-// Householder panel factorisation (larfg + larf over the panel) with the LARFT T factor
-// built in the same pass.
+// Householder panel factorisation (larfg + larf over a panel of at most 32 columns) with the
+// LARFT T factor, one CTA per panel of up to 512 rows: the "owner computes" panel
+// (panel_owner_kernel) of the two-level schedule, plus the pieces the factor-warp and cluster
+// panels share (coalesced staging of the panel through shared memory, the one-warp T).
 //
-// Layout: one warp per panel column. A CTA has 32 warps; warp c owns panel column c, and
-// its lanes hold the CTA's rows of that column, lane l holding local rows l + 32 i
-// (i < RPL). A thread-block cluster of CP CTAs covers a panel taller than 32 * RPL rows,
-// CTA p holding rows [p*R, (p+1)*R), R = 32 * RPL.
-//
-// Reflector j (the loop over columns is a runtime loop: the body is a few hundred bytes):
-//   (a) warp j, whose column already carries every earlier reflector, publishes the
-//       unscaled tail x_j (rows below j, zero elsewhere) in shared memory; lane j of every
-//       warp publishes its row-j value a[j][c];
-//   (b) __syncthreads;
-//   (c) every warp c forms d_c = x_j . a_c over its rows and reduces it across the warp:
-//       c > j gives the trailing dots, c == j gives ||x_j||^2 and c < j gives x_j . v_c,
-//       the LARFT column; for CP > 1 the per-CTA sums are added across the cluster through
-//       distributed shared memory after ONE cluster barrier;
-//   (d) every warp derives beta, tau and scale = 1/(alpha - beta) from alpha = a[j][j] and
-//       ||x_j||^2 (the reference arithmetic, submission.py:91-107); warps c > j apply
-//       a_c -= tau * v_j (v_j^T a_c) with v_j^T a_c = a[j][c] + scale * d_c (the rank-1
-//       update of submission.py:100-103); warp j scales its tail into v_j, stores tau and
-//       appends column j of T: T[i][j] = -tau_j sum_{i<=c<j} T[i][c] z_c,
-//       z_c = v_c^T v_j = a[j][c] + scale * d_c (LARFT, submission.py:129-137).
-// Shared slots are double-buffered by the parity of j, so each reflector costs two CTA
-// barriers (one of them the cluster barrier when CP > 1) and no extra Gram pass.
+// Reflector j (reference arithmetic, submission.py:91-107 for larfg, :100-103 for the rank-1
+// update, :129-137 for LARFT): beta = -sign(alpha) ||(alpha, x)||, tau = (beta - alpha)/beta,
+// v = (1, x / (alpha - beta)); every later column c gets a_c -= tau v (v^T a_c).
 #pragma once
-
-#include <cooperative_groups.h>
 
 #include "common.cuh"
 
 namespace qrb200 {
 
-namespace cg = cooperative_groups;
-
 constexpr int kPanelW = 32;        // panel width (columns) == warps per panel CTA
-constexpr int kPanelThreads = 1024;
 
 struct PanelParams {
   const float* src;       // panel source matrix batch (A for the first panel, else H)
@@ -119,17 +97,6 @@ __device__ __forceinline__ void panel_stage_out(float* __restrict__ Hb, int n, i
   }
 }
 
-template <int RPL>
-struct PanelShared {
-  float xs[2][32 * RPL];                // broadcast tail x_j of the pivot column
-  __align__(16) float rowj[2][32];      // row j of the panel
-  __align__(16) float dsum[2][32];      // per-column dot totals
-  __align__(16) float slot[2][64];      // cluster-visible partials: [column dots | pivot row]
-  float tau[32];           // reflector coefficients (CTA 0)
-  float G[32][33];         // G[c][j] = v_c . v_j, c < j (CTA 0)
-  float T[32][33];         // T factor (CTA 0)
-};
-
 // T of a 32-column panel by one warp from the Gram entries G[c][i] = v_c . v_i (c < i) and
 // tau: T^-1 = diag(1/tau) + striu(V^T V) (the compact-WY factor of H_0 .. H_{k-1}, cf. the LARFT
 // recurrence of submission.py:129-137, which builds the same T column by column). Lane j solves
@@ -153,125 +120,6 @@ __device__ __forceinline__ void larft_inverse_warp(float (&T)[32][33], const flo
   }
 }
 
-// Factor the panel whose column `warp` this warp holds in a[] (rows lane + 32 i of the
-// CTA's row block, p = cluster rank). All threads of the CTA -- and of the cluster when
-// cluster_size > 1 -- must call this with the same (w, jmax).
-template <int RPL, bool HAS_T>
-__device__ __forceinline__ void factor_panel_cols(float (&a)[RPL], const int w, const int jmax,
-                                                  PanelShared<RPL>& sh, float* __restrict__ tau_out,
-                                                  const int cluster_size, const int p) {
-  const int lane = threadIdx.x & 31, c = threadIdx.x >> 5;
-  const int lr0 = p * 32 * RPL + lane;  // local panel row of a[0]
-  cg::cluster_group cluster = cg::this_cluster();
-
-  for (int j = 0; j < jmax; ++j) {
-    const int ph = j & 1;
-    // (a) publish x_j and row j.
-    if (c == j) {
-#pragma unroll
-      for (int i = 0; i < RPL; ++i) sh.xs[ph][lane + 32 * i] = (lr0 + 32 * i > j) ? a[i] : 0.f;
-    }
-    if (p == 0 && lane == j) sh.rowj[ph][c] = a[0];
-    __syncthreads();
-    // (c) d_c = x_j . a_c
-    float x[RPL];
-    float d = 0.f;
-#pragma unroll
-    for (int i = 0; i < RPL; ++i) {
-      x[i] = sh.xs[ph][lane + 32 * i];
-      d = fmaf(x[i], a[i], d);
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) d += __shfl_xor_sync(kFullMask, d, o);
-    float xn2, alpha, ajc;
-    if (cluster_size == 1) {
-      if (lane == 0) sh.dsum[ph][c] = d;
-      __syncthreads();
-      xn2 = sh.dsum[ph][j];
-      alpha = sh.rowj[ph][j];
-      ajc = sh.rowj[ph][c];
-    } else {
-      if (lane == 0) {
-        sh.slot[ph][c] = d;
-        sh.slot[ph][32 + c] = (p == 0) ? sh.rowj[ph][c] : 0.f;
-      }
-      cluster.sync();
-      // One warp gathers the cluster in a single DSMEM round trip: lane l reads columns
-      // 16 (l % 2) .. +15 of CTA l / 2's partial dots (four 16-byte loads; clusters of up to 16
-      // CTAs), the sums over CTAs are formed with four xor shuffles, and lanes 0..1 also fetch
-      // the pivot row from CTA 0. Totals are published in this CTA's shared memory.
-      if (c == 0) {
-        const int q = lane >> 1, cg = lane & 1;
-        float4 v[4], pr[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) v[t] = pr[t] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < cluster_size) {
-          const float* rq = cluster.map_shared_rank(&sh.slot[ph][0], q) + 16 * cg;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) v[t] = *reinterpret_cast<const float4*>(rq + 4 * t);
-        }
-        if (q == 0) {
-          const float* r0 = cluster.map_shared_rank(&sh.slot[ph][0], 0) + 32 + 16 * cg;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) pr[t] = *reinterpret_cast<const float4*>(r0 + 4 * t);
-        }
-#pragma unroll
-        for (int o = 2; o <= 16; o <<= 1) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            v[t].x += __shfl_xor_sync(kFullMask, v[t].x, o);
-            v[t].y += __shfl_xor_sync(kFullMask, v[t].y, o);
-            v[t].z += __shfl_xor_sync(kFullMask, v[t].z, o);
-            v[t].w += __shfl_xor_sync(kFullMask, v[t].w, o);
-          }
-        }
-        if (q == 0) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            *reinterpret_cast<float4*>(&sh.dsum[ph][16 * cg + 4 * t]) = v[t];
-            *reinterpret_cast<float4*>(&sh.rowj[ph][16 * cg + 4 * t]) = pr[t];
-          }
-        }
-      }
-      __syncthreads();
-      d = sh.dsum[ph][c];
-      xn2 = sh.dsum[ph][j];
-      alpha = sh.rowj[ph][j];
-      ajc = sh.rowj[ph][c];
-    }
-    // (d) reflector and updates.
-    const Reflector rf = make_reflector(alpha, xn2);
-    if (c > j && c < w) {
-      const float wc = fmaf(rf.scale, d, ajc);
-      const float cx = rf.tau * rf.scale * wc;
-#pragma unroll
-      for (int i = 0; i < RPL; ++i) {
-        const int lr = lr0 + 32 * i;
-        if (lr > j) a[i] = fmaf(-cx, x[i], a[i]);
-        else if (lr == j) a[i] = fmaf(-rf.tau, wc, a[i]);
-      }
-    } else if (c == j) {
-#pragma unroll
-      for (int i = 0; i < RPL; ++i) {
-        const int lr = lr0 + 32 * i;
-        if (lr > j) a[i] *= rf.scale;
-        else if (lr == j) a[i] = rf.diag;
-      }
-      if (p == 0 && lane == 0) {
-        tau_out[j] = rf.tau;
-        sh.tau[j] = rf.tau;
-      }
-    } else if (HAS_T && c < j && p == 0 && lane == 0) {
-      sh.G[c][j] = fmaf(rf.scale, d, ajc);  // v_c . v_j = a[j][c] + scale * (x_j . v_c)
-    }
-  }
-  if (HAS_T && p == 0) {
-    __syncthreads();
-    if (c == 0) larft_inverse_warp(sh.T, sh.G, sh.tau, jmax);
-  }
-}
-
-// Single-CTA panel, "owner computes" form: used when the whole panel fits one CTA.
 // NW = 32 / CPW warps; warp g owns columns g + NW q (q < CPW), interleaved so that the
 // still-active columns stay spread over all warps. Reflector j:
 //   the owner warp (j % NW) reduces ||x_j||^2 over its column, computes beta, tau and the
@@ -455,48 +303,6 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 12 ? 3 : 
     const int t0 = HAS_T ? (int)threadIdx.x - 32 : (int)threadIdx.x;
     panel_stage_out(Hb, n, k, 0, R, min(R, m), w, stage, HAS_T ? 32 * NW - 32 : 32 * NW, t0);
   }
-}
-
-template <int RPL, bool HAS_T>
-__global__ void __launch_bounds__(kPanelThreads) panel_factor_kernel(PanelParams P) {
-  constexpr int R = 32 * RPL;
-  __shared__ PanelShared<RPL> sh;
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
-  float* stage = reinterpret_cast<float*>(smem_raw);  // 32 x (R + 1) floats
-  cg::cluster_group cluster = cg::this_cluster();
-  const int CP = (int)cluster.num_blocks();
-  const int p = (int)cluster.block_rank();
-  const int bidx = blockIdx.y;
-  const int lane = threadIdx.x & 31, c = threadIdx.x >> 5;
-  const int n = P.n, k = P.k, w = P.w;
-  const int m = n - k;
-  const int r0 = p * R;
-  const int rows_valid = max(0, min(R, m - r0));
-  const float* __restrict__ S = P.src + (long long)bidx * P.src_bstride;
-  float* __restrict__ Hb = P.H + (long long)bidx * n * n;
-
-  if (HAS_T)
-    for (int i = threadIdx.x; i < 32 * 33; i += kPanelThreads) (&sh.T[0][0])[i] = 0.f;
-  panel_stage_in<R, kPanelThreads>(S, n, k, r0, rows_valid, w, stage);
-  __syncthreads();
-  float a[RPL];
-#pragma unroll
-  for (int i = 0; i < RPL; ++i) a[i] = stage[c * (R + 1) + lane + 32 * i];
-  if (CP > 1) cluster.sync();  // every CTA of the cluster runs before any DSMEM access
-  __syncthreads();
-
-  factor_panel_cols<RPL, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k, CP, p);
-
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < RPL; ++i) stage[c * (R + 1) + lane + 32 * i] = a[i];
-  __syncthreads();
-  panel_stage_out(Hb, n, k, r0, R, rows_valid, w, stage, kPanelThreads);
-  if (HAS_T && P.T != nullptr && p == 0) {
-    float* Tb = P.T + (long long)bidx * P.t_bstride;
-    for (int i = threadIdx.x; i < 32 * 32; i += kPanelThreads) Tb[i] = sh.T[i / 32][i % 32];
-  }
-  if (CP > 1) cluster.sync();  // keep this CTA's shared memory alive for remote readers
 }
 
 template <int RPL>

@@ -40,7 +40,6 @@ namespace qrb200 {
 constexpr int kClWarps = 8;
 constexpr int kClThreads = 32 * kClWarps;
 constexpr int kClMaxCta = 16;
-constexpr int kDevStatusClusterTimeout = 7;
 // Row stride of the partial-dot slots: 36 floats put the 16 source rows on different banks, so
 // the lane-parallel totals read them without conflicts (a 32-float stride put them all on one).
 constexpr int kClSlotLd = 36;
@@ -60,13 +59,6 @@ __device__ __forceinline__ uint32_t cl_map(const void* local, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
   return r;
-}
-__device__ __forceinline__ void cl_st4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-__device__ __forceinline__ void cl_arrive(uint32_t mbar_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mbar_addr) : "memory");
 }
 __device__ __forceinline__ void cl_fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -95,7 +87,7 @@ __device__ __forceinline__ bool cl_wait(uint64_t* mbar, uint32_t parity) {
         : "memory");
     if (done) return true;
   }
-  atomicExch(&g_device_status, kDevStatusClusterTimeout);
+  report_device_failure(kSiteCluster);
   return false;
 }
 
@@ -106,10 +98,9 @@ __device__ __forceinline__ void cl_barrier_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// ASYNC: partials travel by st.async and complete transaction bytes on the receiver's
-// mbarrier (one local expect_tx arrival per phase); otherwise plain remote stores followed by
-// a release arrive of every pushing lane.
-template <int RPL, bool ASYNC>
+// Partials travel by st.async and complete transaction bytes on the receiver's mbarrier (one
+// local expect_tx arrival per phase).
+template <int RPL>
 __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
   griddep_launch_wait();
   constexpr int R = 32 * RPL;
@@ -132,13 +123,11 @@ __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
   // Bytes one step brings into this CTA: 16 per warp of every CTA, plus CTA 0's row j.
   const uint32_t step_bytes = (uint32_t)(16 * kClWarps * (CP + 1));
   if (threadIdx.x == 0) {
-    mbar_init(&sh.mbar[0], ASYNC ? 1 : kClWarps * CP);
-    mbar_init(&sh.mbar[1], ASYNC ? 1 : kClWarps * CP);
+    mbar_init(&sh.mbar[0], 1);
+    mbar_init(&sh.mbar[1], 1);
     cl_fence_mbar_init();
-    if (ASYNC) {
-      if (jmax > 0) cl_expect_tx(&sh.mbar[0], step_bytes);
-      if (jmax > 1) cl_expect_tx(&sh.mbar[1], step_bytes);
-    }
+    if (jmax > 0) cl_expect_tx(&sh.mbar[0], step_bytes);
+    if (jmax > 1) cl_expect_tx(&sh.mbar[1], step_bytes);
   }
   // Entry barrier split around the panel load: peers may push only after every CTA's
   // mbarriers are initialised.
@@ -191,21 +180,15 @@ __global__ void __launch_bounds__(kClThreads) panel_cl_kernel(PanelParams P) {
     if (ok && lane < (int)CP) {
       const uint32_t base = cl_map(&sh.slot[ph][0][0], (uint32_t)lane) + my_slot_off;
       const uint32_t rmbar = cl_map(&sh.mbar[ph], (uint32_t)lane);
-      if (ASYNC) {
-        cl_st4_async(base, d[0], d[1], d[2], d[3], rmbar);
-        if (top) cl_st4_async(cl_map(&sh.rowv[ph][4 * g], (uint32_t)lane), rj[0], rj[1], rj[2], rj[3], rmbar);
-      } else {
-        cl_st4(base, d[0], d[1], d[2], d[3]);
-        if (top) cl_st4(cl_map(&sh.rowv[ph][4 * g], (uint32_t)lane), rj[0], rj[1], rj[2], rj[3]);
-        cl_arrive(rmbar);
-      }
+      cl_st4_async(base, d[0], d[1], d[2], d[3], rmbar);
+      if (top) cl_st4_async(cl_map(&sh.rowv[ph][4 * g], (uint32_t)lane), rj[0], rj[1], rj[2], rj[3], rmbar);
     }
     // (3) totals: lane s adds source CTA s's partials; a 4-level butterfly leaves the sum over
     //     all sources, in one fixed order, in every lane of every warp.
     if (ok) ok = cl_wait(&sh.mbar[ph], (uint32_t)((j >> 1) & 1));
     // The phase of step j is complete for every thread of this CTA: the mbarrier's next phase
     // (step j + 2) cannot complete before this CTA's step-(j+1) pushes, so arming it now is safe.
-    if (ASYNC && ok && threadIdx.x == 0 && j + 2 < jmax) cl_expect_tx(&sh.mbar[ph], step_bytes);
+    if (ok && threadIdx.x == 0 && j + 2 < jmax) cl_expect_tx(&sh.mbar[ph], step_bytes);
     const int j1 = min(j + 1, 31);
     const float4 rv = *reinterpret_cast<const float4*>(&sh.rowv[ph][4 * g]);
     const float alpha = sh.rowv[ph][j];

@@ -1,11 +1,16 @@
-// qrb200 C ABI: argument checking, workspace layout and the per-panel launch schedule.
+// qrb200 C ABI: argument checking, workspace layout, the launch schedules and the device
+// failure word.
 //
-// Schedule (right-looking blocked Householder, panel width NB = 32), per panel k:
-//   panel_factor_kernel  -- cluster of CP CTAs per matrix, panel + tau + T      (1 launch)
-//   trailing update      -- C <- C - V T^T V^T C on the columns right of the panel
-//                           (wy_vtc / wy_tw / wy_upd, 3 launches)
-// Small matrices (n <= 64) are factored whole by one CTA in a single launch (the panel
-// kernel with the panel width equal to n), which is the fused one-CTA-per-matrix path.
+// Schedules, chosen by the matrix order n only (so a matrix's result, bit for bit, does not
+// depend on the batch it is factored in):
+//   n <= 128          one CTA per matrix factors the whole matrix in one launch (small_fw);
+//   129 <= n <= 1024  two-level: 128-column outer blocks of four 32-column panels, narrow FP32
+//                     updates inside the block, one 128-wide tcgen05 (3xTF32) update of the
+//                     trailing matrix per block, its far part on a look-ahead stream;
+//   n >= 1025         single-level: 32-column panels (cluster panels above 512 rows), the next
+//                     panel's columns updated on a high-priority stream (U1), the rest (U2) on
+//                     a low-priority one beside the next panel;
+//   rows not 16-byte aligned (n % 4 != 0 or an unaligned input): single-level, one stream.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -18,17 +23,15 @@
 
 #include "../../include/qrb200.h"
 #include "panel.cuh"
-#include "panel_la.cuh"
 #include "panel_fw.cuh"
 #include "panel_cl.cuh"
-#include "small.cuh"
 #include "small_fw.cuh"
 #include "wy_simt.cuh"
 #include "wy_simt2.cuh"
 #include "wy_u1.cuh"
-#include "wy_tc.cuh"
 #include "wy_tc128.cuh"
 #include "wy_tc128p.cuh"
+#include "apply_q.cuh"
 
 namespace qrb200 {
 
@@ -45,13 +48,15 @@ constexpr int kMaxDevicesSm = 64;
 // while a profiling call is active on this host thread, brackets it with CUDA events and
 // records its algorithmic flops and bytes.
 enum KernelKind {
-  K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD, K_TC_VTC, K_TC_UPD,
-  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_U1, K_NUM_KINDS
+  K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD,
+  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_U1, K_PANEL_CL, K_LARFT, K_FILL, K_NUM_KINDS
 };
 static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw", "wy_upd",
-                                                   "tc_vtc", "tc_upd", "tc_gram", "tbuild", "tc_ygemm", "tc_vtc128",
-                                                   "tc_upd128", "wy_u1"};
-static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 1, 1, 1, 1, 1, 1, 0, 1, 1, 1, 0};
+                                                   "tc_gram", "tbuild", "tc_ygemm", "tc_vtc128", "tc_upd128",
+                                                   "wy_u1", "panel_cluster", "larft_blocks", "fill_identity"};
+// 1 = tensor-core contraction (FLOP bound); 0 = FP32 SIMT, memory or latency bound. (wy_vtc
+// counts the 32-wide V^T C, which runs on tcgen05 for wide updates but is HBM bound at K = 32.)
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 0, 0, 0, 1, 0, 1, 1, 1, 0, 0, 0, 0};
 
 static std::atomic<long long> g_launches{0};
 
@@ -102,14 +107,11 @@ static int choose_nsplit(long long /*batch*/, int n, int k, int w) {
   return std::max(1, cdiv(m, kRowsPerSplit));
 }
 
-static int choose_nsplit_tc(long long batch, int m, int nc);
-
 static int max_nsplit(long long batch, int n) {
   int mx = 1;
   for (int k = 0; k < n; k += kNB) {
     const int w = std::min(kNB, n - k);
     mx = std::max(mx, choose_nsplit(batch, n, k, w));
-    if (n - k - w > 0) mx = std::max(mx, choose_nsplit_tc(batch, n - k, n - k - w));
   }
   return mx;
 }
@@ -128,27 +130,14 @@ struct Workspace {
 
 constexpr int kRowsPerSplitWide = 512;  // row split of the 128-wide products (panel height only)
 
-// Two-level (128-column outer blocks on the tensor cores) whenever the matrix is large enough
-// and its rows are 16-byte aligned; QRB200_TWO_LEVEL=0 selects the single-level path.
+// Two-level (128-column outer blocks on the tensor cores) for 129 <= n <= 1024 with rows
+// 16-byte aligned; single-level with look-ahead from kSingleMinN on (the choice depends on the
+// order only, so results do not depend on the batch).
+constexpr int kSingleMinN = 1025;
 static bool use_two_level(int n, const float* A, long long abs) {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_TWO_LEVEL");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1 && n > kOB && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
+  return n > kOB && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
 }
-
-// Single-level schedule with look-ahead for matrices of order >= QRB200_SINGLE_MIN_N (the
-// choice depends on the order only, so results do not depend on the batch).
-static bool use_single_la(int n) {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_SINGLE_MIN_N");
-    v = e ? atoi(e) : 1025;
-  }
-  return n >= v;
-}
+static bool use_single_la(int n) { return n >= kSingleMinN; }
 
 static Workspace layout(long long batch, int n, void* base) {
   Workspace ws{};
@@ -188,6 +177,31 @@ static int current_device() {
   return cudaGetDevice(&d) == cudaSuccess ? d : 0;
 }
 
+// Mapped pinned host words, one per device ordinal, that the kernels' failure reports also
+// write (g_status_mapped); allocated once per process, registered per device on first use.
+constexpr int kStatusWords = 64;
+static std::mutex g_status_mu;
+static int* g_status_host = nullptr;
+
+static int register_status_word(int dev) {
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_status_host) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, kStatusWords * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess)
+      return QRB200_ERR_CUDA;
+    std::memset(p, 0, kStatusWords * sizeof(int));
+    g_status_host = static_cast<int*>(p);
+  }
+  void* dptr = nullptr;
+  if (cudaHostGetDevicePointer(&dptr, g_status_host + dev, 0) != cudaSuccess) return QRB200_ERR_CUDA;
+  int* word = static_cast<int*>(dptr);
+  if (cudaMemcpyToSymbol(g_status_mapped, &word, sizeof(word)) != cudaSuccess) return QRB200_ERR_CUDA;
+  return QRB200_OK;
+}
+
+// The current device must be an sm_100 GPU. The first call per device also registers its
+// mapped failure word (a synchronous symbol copy: make the first call on a device before any
+// stream capture on it).
 static int check_device() {
   static PerDevice ok, bad;
   int dev = 0;
@@ -196,22 +210,16 @@ static int check_device() {
   if (bad.done(dev)) return QRB200_ERR_DEVICE;
   int major = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return QRB200_ERR_CUDA;
-  if (major == 10) {
-    ok.mark(dev);
-    return QRB200_OK;
+  if (major != 10) {
+    bad.mark(dev);
+    return QRB200_ERR_DEVICE;
   }
-  bad.mark(dev);
-  return QRB200_ERR_DEVICE;
-}
-
-// QRB200_PDL=0 launches the single-level chain kernels without programmatic dependent launch.
-static bool pdl_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_PDL");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
+  if (dev < kStatusWords) {
+    const int st = register_status_word(dev);
+    if (st != QRB200_OK) return st;
   }
-  return v == 1;
+  ok.mark(dev);
+  return QRB200_OK;
 }
 
 // Launch with an optional cluster shape and, for kernels that begin with griddep_launch_wait(),
@@ -234,7 +242,7 @@ static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
-  if (pdl && pdl_enabled()) {
+  if (pdl) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -244,60 +252,11 @@ static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int RPL, bool HAS_T>
-static cudaError_t launch_panel(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
-  static PerDevice configured;
-  const int dev = current_device();
-  if (!configured.done(dev)) {
-    cudaError_t e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)panel_stage_bytes<RPL>());
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(panel_factor_kernel<RPL, HAS_T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    configured.mark(dev);
-  }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)cluster, (unsigned)batch, 1);
-  cfg.blockDim = dim3(kPanelThreads, 1, 1);
-  cfg.dynamicSmemBytes = panel_stage_bytes<RPL>();
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, panel_factor_kernel<RPL, HAS_T>, pp);
-}
-
-template <int NMAX>
-static cudaError_t launch_small(const float* A, float* H, float* tau, long long batch, int n,
-                                long long abs, cudaStream_t s) {
-  const size_t smem = sizeof(SmallShared<NMAX>);
-  static PerDevice configured;  // per instantiation and device
-  const int dev = current_device();
-  if (!configured.done(dev)) {
-    cudaError_t e = cudaFuncSetAttribute(small_qr_kernel<NMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured.mark(dev);
-  }
-  small_qr_kernel<NMAX><<<(unsigned)batch, kPanelThreads, smem, s>>>(A, abs, H, tau, n);
-  return cudaGetLastError();
-}
-
-// Pause (ns) between the update warps' polls in the whole-matrix kernel (QRB200_FW_POLL_NS,
-// default 50): idle update warps that sleep leave issue slots to the factor warp, whose
-// reflector chain is the kernel's critical path (about 3% faster on C1 than busy polling).
-static int fw_poll_ns() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_FW_POLL_NS");
-    v = e ? atoi(e) : 50;
-    if (v < 0 || v > 1000) v = 50;
-  }
-  return v;
-}
+// Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch: a factor warp
+// fed by update warps (small_fw_kernel). Idle update warps pause kFwPollNs between polls, which
+// leaves issue slots to the factor warp, whose reflector chain is the kernel's critical path
+// (about 3 % faster on C1 than busy polling).
+constexpr int kFwPollNs = 50;
 
 template <int NMAX, int NWL>
 static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long long batch, int n, long long abs,
@@ -310,35 +269,22 @@ static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long lo
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n, fw_poll_ns());
+  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n, kFwPollNs);
   return cudaGetLastError();
 }
 
-// QRB200_SMALL=smem selects the earlier shared-memory whole-matrix kernel.
-static bool small_pipeline() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_SMALL");
-    v = (e && strcmp(e, "smem") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
-// Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch.
 static cudaError_t run_small(const float* A, float* H, float* tau, long long batch, int n,
                              long long abs, cudaStream_t s) {
   LaunchScope ls(K_SMALL, batch * 4.0 * n * (double)n * n / 3.0, batch * 8.0 * n * (double)n);
-  if (small_pipeline()) {
-    if (n <= 32) return launch_small_fw<32, 8>(A, H, tau, batch, n, abs, s);
-    if (n <= 64) return launch_small_fw<64, 16>(A, H, tau, batch, n, abs, s);
-    return launch_small_fw<128, 16>(A, H, tau, batch, n, abs, s);
-  }
-  if (n <= 64) return launch_small<64>(A, H, tau, batch, n, abs, s);
-  return launch_small<128>(A, H, tau, batch, n, abs, s);
+  if (n <= 32) return launch_small_fw<32, 8>(A, H, tau, batch, n, abs, s);
+  if (n <= 64) return launch_small_fw<64, 16>(A, H, tau, batch, n, abs, s);
+  return launch_small_fw<128, 16>(A, H, tau, batch, n, abs, s);
 }
 
-template <int RPL, int CPW>
+// "Owner computes" panel, one CTA per matrix, four columns per warp.
+template <int RPL>
 static cudaError_t launch_owner(const PanelParams& pp, long long batch, cudaStream_t s) {
+  constexpr int CPW = 4;
   static PerDevice configured;
   const int dev = current_device();
   if (!configured.done(dev)) {
@@ -348,39 +294,6 @@ static cudaError_t launch_owner(const PanelParams& pp, long long batch, cudaStre
     configured.mark(dev);
   }
   panel_owner_kernel<RPL, CPW, true><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), panel_stage_bytes<RPL>(), s>>>(pp);
-  return cudaGetLastError();
-}
-
-static int panel_cpw() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_PANEL_CPW");
-    v = e ? atoi(e) : 4;
-    if (v != 1 && v != 2 && v != 4) v = 4;
-  }
-  return v;
-}
-
-template <int RPL>
-static cudaError_t launch_owner_cpw(const PanelParams& pp, long long batch, cudaStream_t s) {
-  switch (panel_cpw()) {
-    case 1: return launch_owner<RPL, 1>(pp, batch, s);
-    case 2: return launch_owner<RPL, 2>(pp, batch, s);
-    default: return launch_owner<RPL, 4>(pp, batch, s);
-  }
-}
-
-template <int RPL, int CPW>
-static cudaError_t launch_la(const PanelParams& pp, long long batch, cudaStream_t s) {
-  static PerDevice configured;
-  const int dev = current_device();
-  if (!configured.done(dev)) {
-    cudaError_t e = cudaFuncSetAttribute(panel_la_kernel<RPL, CPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)panel_stage_bytes<RPL>());
-    if (e != cudaSuccess) return e;
-    configured.mark(dev);
-  }
-  panel_la_kernel<RPL, CPW><<<dim3(1, (unsigned)batch), 32 * (32 / CPW), panel_stage_bytes<RPL>(), s>>>(pp);
   return cudaGetLastError();
 }
 
@@ -398,149 +311,55 @@ static cudaError_t launch_fw(const PanelParams& pp, long long batch, cudaStream_
                   true, pp);
 }
 
-template <int RPL, bool ASYNC>
+template <int RPL>
 static cudaError_t launch_cl(const PanelParams& pp, int cluster, long long batch, cudaStream_t s) {
   static PerDevice configured;
   const int dev = current_device();
   if (!configured.done(dev)) {
-    cudaError_t e = cudaFuncSetAttribute(panel_cl_kernel<RPL, ASYNC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(panel_cl_kernel<RPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)panel_cl_smem<RPL>());
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(panel_cl_kernel<RPL, ASYNC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      e = cudaFuncSetAttribute(panel_cl_kernel<RPL>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  return launch_k(panel_cl_kernel<RPL, ASYNC>, dim3((unsigned)cluster, (unsigned)batch, 1), dim3(kClThreads, 1, 1),
+  return launch_k(panel_cl_kernel<RPL>, dim3((unsigned)cluster, (unsigned)batch, 1), dim3(kClThreads, 1, 1),
                   panel_cl_smem<RPL>(), s, (unsigned)cluster, true, pp);
 }
 
-// Rows per CTA of the cluster panel (QRB200_CL_ROWS = 128, 256 or 512; 0 turns the cluster
-// panel off) and the smallest panel height it takes (QRB200_CL_MIN_M).
-static int cl_rows() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_CL_ROWS");
-    v = e ? atoi(e) : 256;
-    if (v != 0 && v != 128 && v != 256 && v != 512) v = 256;
-  }
-  return v;
-}
-// QRB200_CL_ASYNC=0 exchanges the cluster panel's partials with remote stores and release
-// arrives instead of st.async transactions.
-static bool cl_async() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_CL_ASYNC");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-static int cl_min_m() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_CL_MIN_M");
-    v = e ? atoi(e) : 513;
-  }
-  return v;
-}
+// Panel kernel by panel height m (the choice depends on the matrix order and m only, so
+// results stay independent of the batch):
+//   m >= 513: cluster of ceil(m / 256) CTAs (<= 16), 256 rows each (panel_cl_kernel);
+//   m <= 512, n >= 1025: one CTA with a factor warp fed by update warps (panel_fw_kernel) --
+//     the shorter chain, for the latency-bound launches of a few large matrices;
+//   m <= 512, n <= 1024: the owner-computes panel (three CTAs per SM up to 384 rows), for the
+//     throughput-bound launches of many small matrices.
+constexpr int kClRows = 256;
+constexpr int kClMinM = 513;
+constexpr int kFwMinN = 1025;
 
-// Panels of 513..1024 rows: one CTA with in-panel look-ahead (default), or QRB200_PANEL=owner
-// for the two-CTA cluster panel.
-// QRB200_PANEL_FW=0 keeps the owner-computes panel for panels of up to 512 rows of matrices
-// larger than 512.
-static bool panel_fw() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_PANEL_FW");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
+static bool is_cluster_panel(int m) { return m >= kClMinM && m <= kClMaxCta * kClRows; }
 
-// Smallest matrix order whose panels of up to 512 rows use the factor-warp kernel
-// (QRB200_FW_MIN_N; the owner kernel below it). 1025: the two-level schedule (n <= 1024) keeps
-// the owner panels, which run three CTAs per SM up to 384 rows (C3 about 1 % faster than with
-// the factor-warp panels); the single-level schedule's few large matrices take the factor warp.
-static int fw_min_n() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_FW_MIN_N");
-    v = e ? atoi(e) : 1025;
-  }
-  return v;
-}
-
-static bool panel_lookahead() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_PANEL");
-    v = (e && strcmp(e, "owner") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
-// Panel kernel shape by panel height: panels up to 512 rows are factored by one CTA
-// ("owner computes" form, rows spread over the lanes of each column's warp), panels up to
-// 1024 rows by one CTA of 16 warps with in-panel look-ahead; taller panels use a cluster of
-// ceil(m / 256) CTAs of 32 warps (one per column), at most 16.
 static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batch, cudaStream_t s, long long t_bstride) {
   PanelParams q = pp;
   q.t_bstride = t_bstride;
-  // The factor-warp panel has the shorter chain (latency-bound launches: few, large matrices);
-  // the owner panel fits two CTAs per SM (throughput-bound launches: many small matrices).
-  // The choice depends on the matrix order only, so results stay independent of the batch.
-  const int clr = cl_rows();
-  if (clr > 0 && m >= cl_min_m() && m <= kClMaxCta * clr) {
-    if (cl_async()) {
-      if (clr == 128) return launch_cl<4, true>(q, cdiv(m, 128), batch, s);
-      if (clr == 512) return launch_cl<16, true>(q, cdiv(m, 512), batch, s);
-      return launch_cl<8, true>(q, cdiv(m, 256), batch, s);
-    }
-    if (clr == 128) return launch_cl<4, false>(q, cdiv(m, 128), batch, s);
-    if (clr == 512) return launch_cl<16, false>(q, cdiv(m, 512), batch, s);
-    return launch_cl<8, false>(q, cdiv(m, 256), batch, s);
-  }
-  if (panel_fw() && pp.n >= fw_min_n()) {
+  if (is_cluster_panel(m)) return launch_cl<8>(q, cdiv(m, kClRows), batch, s);
+  if (pp.n >= kFwMinN) {
     if (m <= 128) return launch_fw<4>(q, batch, s);
     if (m <= 256) return launch_fw<8>(q, batch, s);
-    if (m <= 512) return launch_fw<16>(q, batch, s);
+    return launch_fw<16>(q, batch, s);
   }
-  if (m <= 128) return launch_owner_cpw<4>(q, batch, s);
-  if (m <= 256) return launch_owner_cpw<8>(q, batch, s);
-  if (m <= 384) return launch_owner_cpw<12>(q, batch, s);  // three CTAs per SM (two at 16 rows a lane)
-  if (m <= 512) return launch_owner_cpw<16>(q, batch, s);
-  if (m <= 1024 && panel_lookahead()) return launch_la<32, 2>(q, batch, s);
-  if (m <= 1024) return launch_panel<16, true>(q, cdiv(m, 512), batch, s);
-  return launch_panel<8, true>(q, cdiv(m, kPanelRows), batch, s);
+  if (m <= 128) return launch_owner<4>(q, batch, s);
+  if (m <= 256) return launch_owner<8>(q, batch, s);
+  if (m <= 384) return launch_owner<12>(q, batch, s);
+  return launch_owner<16>(q, batch, s);
 }
 
-// Trailing-update implementation for 32-wide panels: CUDA cores (default: at this width the
-// update is bound by HBM traffic, which the FP32 kernels already stream at ~60 % of peak) or
-// the tensor-core kernels (QRB200_WY=tc; needs n % 4 == 0 and 16-byte aligned input).
-static bool use_tc_update(int n, const float* A, long long abs) {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_WY");
-    v = (e && strcmp(e, "tc") == 0) ? 1 : 0;
-  }
-  return v == 1 && (n % 4) == 0 && (abs % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0;
-}
+// Kernel kind of the panel launch for a panel of m rows (cluster panels counted apart).
+static int panel_kind(int m) { return is_cluster_panel(m) ? K_PANEL_CL : K_PANEL; }
 
-static cudaError_t tc_configure() {
-  static PerDevice done;
-  const int dev = current_device();
-  if (done.done(dev)) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(tc_vtc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtcSmem);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(tc_upd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpdSmem);
-  if (e != cudaSuccess) return e;
-  done.mark(dev);
-  return cudaSuccess;
-}
-
-// Row splits of the tensor-core V^T C product (panel height only, see choose_nsplit).
-static int choose_nsplit_tc(long long /*batch*/, int m, int /*nc*/) { return std::max(1, cdiv(m, kRowsPerSplit)); }
-
+// Single-level schedule for rows that are not 16-byte aligned (n % 4 != 0 or an unaligned
+// input, n <= 1024): 32-column panels and the FP32 update of wy_simt.cuh, one stream.
 static cudaError_t run_blocked(const float* A, float* H, float* tau, long long batch, int n,
                                long long abs, const Workspace& ws, cudaStream_t s) {
   const int ncmax = n;
@@ -553,42 +372,11 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
     PanelParams pp{src, sbs, H, tau, nc > 0 ? ws.T : nullptr, n, k, w};
     cudaError_t e;
     {
-      LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+      LaunchScope ls(panel_kind(m), batch * panel_flops(m, w), batch * 8.0 * m * w);
       e = launch_panel_for(pp, m, batch, s, kNB * kNB);
     }
     if (e != cudaSuccess) return e;
     if (nc <= 0) continue;
-    if (use_tc_update(n, A, abs)) {
-      e = tc_configure();
-      if (e != cudaSuccess) return e;
-      WyParams wp{};
-      wp.src = src;
-      wp.src_bstride = sbs;
-      wp.H = H;
-      wp.T = ws.T;
-      wp.t_bstride = kNB * kNB;
-      wp.Wp = ws.Wp;
-      wp.n = n;
-      wp.k = k;
-      wp.w = w;
-      wp.cend = n;
-      wp.nsplit = choose_nsplit_tc(batch, m, nc);
-      wp.rows_per_split = kRowsPerSplit;
-      wp.ncmax = ncmax;
-      const double bm = (double)batch * m;
-      {
-        LaunchScope ls(K_TC_VTC, 2.0 * bm * w * nc, 4.0 * bm * (w + nc) + 4.0 * batch * wp.nsplit * w * (double)nc);
-        tc_vtc_kernel<<<dim3(cdiv(nc, kTcCols), wp.nsplit, (unsigned)batch), 128, kVtcSmem, s>>>(wp);
-      }
-      {
-        LaunchScope ls(K_TC_UPD, 2.0 * bm * w * nc + (double)batch * w * w * nc,
-                       8.0 * bm * nc + 4.0 * bm * w + 4.0 * batch * wp.nsplit * w * (double)nc);
-        tc_upd_kernel<<<dim3(cdiv(nc, kTcCols), cdiv(m, kTcRows), (unsigned)batch), 128, kUpdSmem, s>>>(wp);
-      }
-      e = cudaGetLastError();
-      if (e != cudaSuccess) return e;
-      continue;
-    }
     WyParams wp{};
     wp.src = src;
     wp.src_bstride = sbs;
@@ -623,113 +411,27 @@ static cudaError_t run_blocked(const float* A, float* H, float* tau, long long b
   return cudaSuccess;
 }
 
-
-// Operand ring of the 128-wide GEMM tiles: QRB200_PIPE = 3 (default: three slots, loads one
-// stage ahead, two CTAs per SM), 4 (four slots, two ahead, one CTA per SM) or 0 (the
-// register-staged kernel).
-static int pipe_slots() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_PIPE");
-    v = e ? atoi(e) : 3;
-    if (v != 0 && v != 3 && v != 4) v = 3;
-  }
-  return v;
-}
-
+// Shared-memory opt-in of the 128-wide tensor-core kernels (three-slot operand rings: two CTAs
+// per SM for the GEMM tiles, four for the Gram) and of tbuild, once per device.
 static cudaError_t tc128_configure() {
   static PerDevice done;
   const int dev = current_device();
   if (done.done(dev)) return cudaSuccess;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_vtcw_kernel<kOB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_smem<kOB>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, false, 3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, true, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, true, 3>())) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, false, 4>())) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<kOB, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcw_pipe_smem<kOB, true, 4>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_Y>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_gemm128_kernel<MODE_UPD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemm128Smem)) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<4>())) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<4>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   done.mark(dev);
   return cudaSuccess;
 }
 
-// QRB200_WY2=0 keeps the first-generation FP32 update kernels for aligned rows too.
-static bool wy2_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_WY2");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
-// QRB200_WY3=0 keeps the 128-column V^T C tiles and the one-tile-per-CTA update.
-static bool wy3_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_WY3");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
-// Narrow updates of the two-level schedule through the one-launch clustered kernel for
-// matrices of order >= QRB200_NARROW_U1_MIN_N (default 1024: it helps at small batch and
-// tall panels, and loses to the streaming kernels at n = 512 and batch 640).
-static bool narrow_u1(int n) {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_NARROW_U1_MIN_N");
-    v = e ? atoi(e) : 1024;
-  }
-  return n >= v;
-}
-
-// Widest update (columns) taken by the one-launch clustered kernel (QRB200_U1_MAX, 0 = off).
-static int u1_max_cols() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_U1_MAX");
-    v = e ? atoi(e) : 128;
-  }
-  return v;
-}
-
-// QRB200_WY4=0 keeps the 64 x 64 update tiles for updates wider than 64 columns.
-static bool wy4_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_WY4");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-// QRB200_NARROW_TILES=0 keeps 128-column V^T C tiles and 64 x 64 update tiles for updates of
-// 32 or 64 columns.
-static bool narrow_tiles() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_NARROW_TILES");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-// QRB200_VTC8X8=1 selects the 8 x 8-per-thread V^T C kernel (measured slower on B200 than the
-// 8 x 4 one at C3 and C5, so off by default).
-static bool wy_vtc8x8() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_VTC8X8");
-    v = (e && strcmp(e, "1") == 0) ? 1 : 0;
-  }
-  return v == 1;
-}
+// Narrow updates of the two-level schedule take the one-launch clustered kernel (wy_u1) for
+// matrices of order >= kNarrowU1MinN (it helps at small batch and tall panels, and loses to the
+// streaming kernels at n = 512 and batch 640); updates of up to kU1MaxCols columns qualify.
+constexpr int kNarrowU1MinN = 1024;
+constexpr int kU1MaxCols = 128;
 
 // Streaming multiprocessors of the current device (cached per device).
 static int num_sms() {
@@ -742,35 +444,13 @@ static int num_sms() {
   return v;
 }
 
-// FP32 compact-WY update of columns [k + w + coff, cend) by the panel at k (the narrow update
-// inside an outer block, or either half of a single-level look-ahead update). T factors sit
-// t_bstride elements apart.
-// Resident CTAs per SM of the wide FP32 update kernel wy_upd4 (QRB200_UPD_PERSIST; default 0:
-// one CTA per tile). A persistent grid (2 per SM) that fills every SM before the next
-// high-priority panel launches keeps that panel waiting until the whole update is done, which
-// made C4 / C5 times bimodal (C4 5.2 or 5.9 ms from one process to the next); one-tile CTAs
-// free SMs continuously and the look-ahead chain's kernels go first.
-static int upd_persist() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_UPD_PERSIST");
-    v = e ? atoi(e) : 0;
-    if (v < 0 || v > 8) v = 0;
-  }
-  return v;
-}
-
-// The wide 32-column V^T C of the single-level schedule on tcgen05 (3xTF32, partials stored
-// transposed, then wy_tw2t; default), or QRB200_U2_TC=0 for the FP32 wy_vtc3 kernel.
-static bool u2_tc() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_U2_TC");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
+// Compact-WY update of columns [k + w + coff, cend) by the 32-column panel at k (the narrow
+// update inside an outer block, or either half of a single-level look-ahead update). T factors
+// sit t_bstride elements apart. Aligned rows: a short update (<= 128 columns, allow_u1) is one
+// clustered launch (wy_u1: V^T C partials per 256-row CTA summed over DSMEM, T^T, update);
+// otherwise V^T C (tcgen05 beyond 128 columns, else FP32), T^T sum, FP32 update with one tile
+// per CTA for wide updates (a persistent grid that filled every SM before the next
+// high-priority panel launched held that panel back). Unaligned rows: wy_simt.cuh.
 static cudaError_t launch_wy(const float* src, long long sbs, float* H, const float* T, long long t_bstride,
                              const Workspace& ws, long long batch, int n, int k, int w, int coff, int cend,
                              cudaStream_t s, bool allow_u1 = false) {
@@ -797,15 +477,13 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   auto note = [&ep](cudaError_t e) {
     if (ep == cudaSuccess) ep = e;
   };
-  const bool vec = wy2_enabled() && w == kNB && (n % 4) == 0 && (sbs % 4) == 0 &&
+  const bool vec = w == kNB && (n % 4) == 0 && (sbs % 4) == 0 &&
                    ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(H)) & 15u) == 0;
   if (vec) {
     static PerDevice configured;
     const int dev = current_device();
     if (!configured.done(dev)) {
       cudaError_t e = cudaFuncSetAttribute(wy_vtc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc2Smem);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(wy_vtc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_upd3_kernel<kU3Rows, kU3Cols>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)upd3_smem<kU3Rows, kU3Cols>());
@@ -816,15 +494,15 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_vtcn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)vtcn_smem<64>());
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(wy_vtc4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVtc3Smem);
-      if (e == cudaSuccess)
         e = cudaFuncSetAttribute(wy_upd4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kUpd4Smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<32, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)vtcw_pipe_smem<32, false, 3>());
       if (e != cudaSuccess) return e;
       configured.mark(dev);
     }
   }
-  if (allow_u1 && vec && ncl <= u1_max_cols() && m <= kClMaxCta * kU1Rows) {
-    // Short update: one clustered launch (V^T C, T^T and the update together).
+  if (allow_u1 && vec && ncl <= kU1MaxCols && m <= kClMaxCta * kU1Rows) {
     static PerDevice configured_u1;
     const int dev = current_device();
     if (!configured_u1.done(dev)) {
@@ -838,42 +516,20 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(256), kU1Smem, s,
                     (unsigned)cp, true, wp);
   }
-  const bool vtc_tc = vec && u2_tc() && ncl > kV2Cols && wy3_enabled();
-  if (vtc_tc) {
-    static PerDevice configured_tc;
-    const int dev = current_device();
-    if (!configured_tc.done(dev)) {
-      cudaError_t e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<32, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)vtcw_pipe_smem<32, false, 3>());
-      if (e != cudaSuccess) return e;
-      configured_tc.mark(dev);
-    }
-  }
-  if (vtc_tc) {
+  const bool vtc_tc = vec && ncl > kV2Cols;  // wide V^T C on tcgen05, partials stored transposed
+  {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
-    tc_vtcw_pipe_kernel<32, false, 3><<<dim3(cdiv(ncl, kTcCols), wp.nsplit, (unsigned)batch), 128,
-                                         vtcw_pipe_smem<32, false, 3>(), s>>>(wp);
-  } else if (vec) {
-    LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
-    if (ncl > kV2Cols && wy3_enabled())
-    {
-      if (wy_vtc8x8())
-        wy_vtc4_kernel<<<dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), 128, kVtc3Smem, s>>>(wp);
-      else
-        note(launch_k(wy_vtc3_kernel, dim3(cdiv(ncl, kV3Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc3Smem, s, 0, true, wp));
-    }
+    if (vtc_tc)
+      tc_vtcw_pipe_kernel<32, false, 3><<<dim3(cdiv(ncl, kTcCols), wp.nsplit, (unsigned)batch), 128,
+                                          vtcw_pipe_smem<32, false, 3>(), s>>>(wp);
+    else if (vec && ncl <= 32)
+      note(launch_k(wy_vtcn_kernel<32>, dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<32>(), s, 0, true, wp));
+    else if (vec && ncl <= 64)
+      note(launch_k(wy_vtcn_kernel<64>, dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<64>(), s, 0, true, wp));
+    else if (vec)
+      note(launch_k(wy_vtc2_kernel, dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc2Smem, s, 0, true, wp));
     else
-    {
-      if (ncl <= 32 && narrow_tiles())
-        note(launch_k(wy_vtcn_kernel<32>, dim3(cdiv(ncl, 32), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<32>(), s, 0, true, wp));
-      else if (ncl <= 64 && narrow_tiles())
-        note(launch_k(wy_vtcn_kernel<64>, dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), dim3(256), vtcn_smem<64>(), s, 0, true, wp));
-      else
-        note(launch_k(wy_vtc2_kernel, dim3(cdiv(ncl, kV2Cols), wp.nsplit, (unsigned)batch), dim3(256), kVtc2Smem, s, 0, true, wp));
-    }
-  } else {
-    LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
-    wy_vtc_kernel<kNB><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
+      wy_vtc_kernel<kNB><<<dim3(cdiv(ncl, 64), wp.nsplit, (unsigned)batch), 256, 0, s>>>(wp);
   }
   {
     LaunchScope ls(K_TW, (double)batch * w * w * ncl, 4.0 * batch * (wp.nsplit + 1.0) * w * ncl);
@@ -886,28 +542,23 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
   }
   {
     LaunchScope ls(K_UPD, 2.0 * bm * w * ncl, 8.0 * bm * ncl + 4.0 * bm * w + 4.0 * batch * w * (double)ncl);
-    if (vec && wy3_enabled() && wy4_enabled() && ncl > kU3Cols) {
+    if (vec && ncl > kU3Cols) {
       const int tc = cdiv(ncl, kU4Cols), tr = cdiv(m, kU4Rows);
       const long long nt = (long long)tc * tr * batch;
-      const int pers = upd_persist();
-      const int grid = (int)(pers > 0 ? std::min<long long>(nt, (long long)pers * num_sms()) : nt);
-      note(launch_k(wy_upd4_kernel, dim3(grid), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt));
-    } else if (vec && wy3_enabled()) {
-      if (ncl <= 32 && narrow_tiles()) {
-        const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
-        const long long nt = (long long)tc * tr * batch;
-        const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        note(launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt));
-      } else {
-        const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
-        const long long nt = (long long)tc * tr * batch;
-        const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
-        note(launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt));
-      }
-    } else if (vec)
-      wy_upd2_kernel<<<dim3(cdiv(ncl, kU2Cols), cdiv(m, kU2Rows), (unsigned)batch), 256, 0, s>>>(wp);
-    else
+      note(launch_k(wy_upd4_kernel, dim3((unsigned)nt), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt));
+    } else if (vec && ncl <= 32) {
+      const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
+      const long long nt = (long long)tc * tr * batch;
+      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+      note(launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt));
+    } else if (vec) {
+      const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
+      const long long nt = (long long)tc * tr * batch;
+      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+      note(launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt));
+    } else {
       wy_upd_kernel<kNB><<<dim3(cdiv(ncl, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
+    }
   }
   return ep != cudaSuccess ? ep : cudaGetLastError();
 }
@@ -924,8 +575,8 @@ constexpr int kMaxDevices = 64;
 // One set of look-ahead streams per caller stream (up to kLaSlots per device), so calls enqueued
 // on different streams -- the host API's batch pieces, or several host threads -- factor
 // concurrently instead of queueing behind one shared pair. Calls on one caller stream reuse its
-// set and stay ordered; its mutex keeps one enqueue at a time on a set. Beyond kLaSlots caller
-// streams, sets are shared (and those calls serialised), which stays correct.
+// set and stay ordered; its mutex keeps one enqueue at a time on a set. Callers beyond the
+// first kLaSlots streams of a device run without look-ahead (la_slot).
 constexpr int kLaSlots = 8;
 struct LaSlot {
   std::mutex mu;
@@ -936,19 +587,23 @@ struct LaSlot {
 static std::mutex g_la_table_mu[kMaxDevices];
 static LaSlot g_la_slots[kMaxDevices][kLaSlots];
 
-static LaSlot& la_slot(int dev, cudaStream_t s) {
+// The caller stream's slot, or nullptr once kLaSlots other caller streams hold every slot of
+// the device (slots are never released: a stream handle may be destroyed and reused). Such a
+// call runs its schedule serially on the caller's stream: no look-ahead, but no stream shared
+// with another caller either (which would order, or -- under stream capture -- invalidate,
+// that caller's work).
+static LaSlot* la_slot(int dev, cudaStream_t s) {
   std::lock_guard<std::mutex> lk(g_la_table_mu[dev]);
   LaSlot* free_slot = nullptr;
   for (LaSlot& sl : g_la_slots[dev]) {
-    if (sl.used && sl.owner == s) return sl;
+    if (sl.used && sl.owner == s) return &sl;
     if (!sl.used && free_slot == nullptr) free_slot = &sl;
   }
   if (free_slot != nullptr) {
     free_slot->used = true;
     free_slot->owner = s;
-    return *free_slot;
   }
-  return g_la_slots[dev][(reinterpret_cast<uintptr_t>(s) >> 4) % kLaSlots];
+  return free_slot;
 }
 
 static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
@@ -969,16 +624,6 @@ static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
   return cudaSuccess;
 }
 
-// QRB200_LOOKAHEAD=0 keeps the whole two-level schedule on the caller's stream.
-static bool lookahead_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("QRB200_LOOKAHEAD");
-    v = (e && strcmp(e, "0") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
 // 128-wide update of trailing columns [coff, cend - k0 - ow) (relative to k0 + ow) by the
 // outer block at k0: W^T = C^T V per row split, then C -= Y W. coff is a multiple of 128, so
 // every column sees the same tiles, and the same arithmetic, however the range is cut.
@@ -987,6 +632,7 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   const int m = n - k0, nc = cend - k0 - ow - coff;
   if (nc <= 0) return cudaSuccess;
   const int nsw = cdiv(m, kRowsPerSplitWide);
+  if (nsw > 2) return cudaErrorInvalidValue;  // the update tile sums at most two W^T partials
   const double bm = (double)batch * m;
   WyParams wp{};
   wp.src = src;
@@ -1020,22 +666,12 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   {
     LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
     const dim3 grid(cdiv(nc, kTcCols), nsw, (unsigned)batch);
-    switch (pipe_slots()) {
-      case 3: tc_vtcw_pipe_kernel<kOB, false, 3><<<grid, 128, vtcw_pipe_smem<kOB, false, 3>(), s>>>(wp); break;
-      case 4: tc_vtcw_pipe_kernel<kOB, false, 4><<<grid, 128, vtcw_pipe_smem<kOB, false, 4>(), s>>>(wp); break;
-      default: tc_vtcw_kernel<kOB, false><<<grid, 128, vtcw_smem<kOB>(), s>>>(wp);
-    }
+    tc_vtcw_pipe_kernel<kOB, false, 3><<<grid, 128, vtcw_pipe_smem<kOB, false, 3>(), s>>>(wp);
   }
   {
     LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
     const dim3 grid(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch);
-    const int ps = pipe_slots();
-    if (ps == 4 && nsw <= 2)
-      tc_gemm128_pipe_kernel<MODE_UPD, 4><<<grid, 128, pipe128_smem<4>(), s>>>(gp);
-    else if (ps == 3 && nsw <= 2)
-      tc_gemm128_pipe_kernel<MODE_UPD, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
-    else
-      tc_gemm128_kernel<MODE_UPD><<<grid, 128, kGemm128Smem, s>>>(gp);
+    tc_gemm128_pipe_kernel<MODE_UPD, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
   }
   return cudaGetLastError();
 }
@@ -1061,12 +697,12 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
       // panel factors land in slot b of the batch x 4 x 32 x 32 array
       PanelParams pp{src, sbs, H, tau, Tslot, n, kb, w};
       {
-        LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+        LaunchScope ls(panel_kind(m), batch * panel_flops(m, w), batch * 8.0 * m * w);
         e = launch_panel_for(pp, m, batch, sp, 4 * kNB * kNB);
       }
       if (e != cudaSuccess) return e;
       if (kb + w < k0 + ow) {
-        e = launch_wy(src, sbs, H, Tslot, 4 * kNB * kNB, ws, batch, n, kb, w, 0, k0 + ow, sp, narrow_u1(n));
+        e = launch_wy(src, sbs, H, Tslot, 4 * kNB * kNB, ws, batch, n, kb, w, 0, k0 + ow, sp, n >= kNarrowU1MinN);
         if (e != cudaSuccess) return e;
       }
     }
@@ -1093,11 +729,7 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
     {
       LaunchScope ls(K_GRAM, 2.0 * bm * ow * ow, 4.0 * bm * ow);
       const dim3 grid(1, nsw, (unsigned)batch);
-      switch (pipe_slots()) {
-        case 3: tc_vtcw_pipe_kernel<kOB, true, 3><<<grid, 128, vtcw_pipe_smem<kOB, true, 3>(), sp>>>(g); break;
-        case 4: tc_vtcw_pipe_kernel<kOB, true, 4><<<grid, 128, vtcw_pipe_smem<kOB, true, 4>(), sp>>>(g); break;
-        default: tc_vtcw_kernel<kOB, true><<<grid, 128, vtcw_smem<kOB>(), sp>>>(g);
-      }
+      tc_vtcw_pipe_kernel<kOB, true, 3><<<grid, 128, vtcw_pipe_smem<kOB, true, 3>(), sp>>>(g);
     }
     {
       TbuildParams tp{ws.Gp, nsw, ws.T, ws.Tob, ow};
@@ -1115,13 +747,7 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
     {
       LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
       const dim3 grid(1, cdiv(m, 128), (unsigned)batch);
-      const int ps = pipe_slots();
-      if (ps == 4)
-        tc_gemm128_pipe_kernel<MODE_Y, 4><<<grid, 128, pipe128_smem<4>(), sp>>>(gp);
-      else if (ps == 3)
-        tc_gemm128_pipe_kernel<MODE_Y, 3><<<grid, 128, pipe128_smem<3>(), sp>>>(gp);
-      else
-        tc_gemm128_kernel<MODE_Y><<<grid, 128, kGemm128Smem, sp>>>(gp);
+      tc_gemm128_pipe_kernel<MODE_Y, 3><<<grid, 128, pipe128_smem<3>(), sp>>>(gp);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const int split_at = k0 + 2 * kOB;  // U1 = columns [k0 + ow, split_at), U2 = [split_at, n)
@@ -1150,12 +776,13 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
   const int dev = current_device();
   // Serial schedule when profiling (per-launch events on one stream), when switched off, or
   // when no outer block has columns beyond the next one (n <= 256).
-  if (t_prof || !lookahead_enabled() || n <= 2 * kOB || dev >= kMaxDevices)
+  if (t_prof || n <= 2 * kOB || dev >= kMaxDevices)
     return two_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
-  LaSlot& slot = la_slot(dev, s);
-  std::lock_guard<std::mutex> lk(slot.mu);
+  LaSlot* slot = la_slot(dev, s);
+  if (slot == nullptr) return two_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
+  std::lock_guard<std::mutex> lk(slot->mu);
   LookaheadStreams* L = nullptr;
-  if ((e = lookahead_streams(slot, &L)) != cudaSuccess) return e;
+  if ((e = lookahead_streams(*slot, &L)) != cudaSuccess) return e;
   if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
@@ -1186,7 +813,7 @@ static cudaError_t single_level_body(const float* A, float* H, float* tau, long 
     float* Tslot = ws.T + (size_t)((kb / kNB) & 1) * kNB * kNB;
     PanelParams pp{src, sbs, H, tau, nc > 0 ? Tslot : nullptr, n, kb, w};
     {
-      LaunchScope ls(K_PANEL, batch * panel_flops(m, w), batch * 8.0 * m * w);
+      LaunchScope ls(panel_kind(m), batch * panel_flops(m, w), batch * 8.0 * m * w);
       e = launch_panel_for(pp, m, batch, sp, kTStride);
     }
     if (e != cudaSuccess) return e;
@@ -1218,11 +845,12 @@ static cudaError_t single_level_body(const float* A, float* H, float* tau, long 
 // look-ahead streams, both joined back into the caller's stream (also after a failed launch).
 template <class Body>
 static cudaError_t with_lookahead(int dev, cudaStream_t s, Body body) {
-  LaSlot& slot = la_slot(dev, s);
-  std::lock_guard<std::mutex> lk(slot.mu);
+  LaSlot* slot = la_slot(dev, s);
+  if (slot == nullptr) return body(nullptr);
+  std::lock_guard<std::mutex> lk(slot->mu);
   LookaheadStreams* L = nullptr;
   cudaError_t e;
-  if ((e = lookahead_streams(slot, &L)) != cudaSuccess) return e;
+  if ((e = lookahead_streams(*slot, &L)) != cudaSuccess) return e;
   if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
@@ -1237,11 +865,161 @@ static cudaError_t with_lookahead(int dev, cudaStream_t s, Body body) {
 static cudaError_t run_single_la(const float* A, float* H, float* tau, long long batch, int n, long long abs,
                                  const Workspace& ws, cudaStream_t s) {
   const int dev = current_device();
-  if (t_prof || !lookahead_enabled() || n <= 2 * kNB || dev >= kMaxDevices)
+  if (t_prof || n <= 2 * kNB || dev >= kMaxDevices)
     return single_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
   return with_lookahead(dev, s, [&](LookaheadStreams* L) {
+    if (L == nullptr) return single_level_body(A, H, tau, batch, n, abs, ws, s, s, nullptr);
     return single_level_body(A, H, tau, batch, n, abs, ws, L->p, L->u, L);
   });
+}
+
+// ---------------------------------------------------------------------------------------
+// Applying Q / Q^T (sormqr) and forming Q (sorgqr) from (H, tau) on the 128-wide kernels.
+constexpr int kApplyRowsPerSplit = 2048;  // row split of the products: <= 2 splits for n <= 4096
+
+struct ApplyWorkspace {
+  float *Gp, *Tp, *Tob, *Y, *Wf;
+  size_t bytes;
+};
+
+static ApplyWorkspace apply_layout(long long batch, int n, int nrhs, void* base) {
+  ApplyWorkspace ws{};
+  auto carve = [&](size_t bytes) {
+    const size_t off = ws.bytes;
+    ws.bytes += align_up(bytes, 256);
+    return reinterpret_cast<float*>(static_cast<char*>(base) + off);
+  };
+  const size_t f = sizeof(float);
+  const int nsw = cdiv(n, kApplyRowsPerSplit);
+  ws.Gp = carve((size_t)batch * nsw * kOB * kOB * f);
+  ws.Tp = carve((size_t)batch * 4 * kNB * kNB * f);
+  ws.Tob = carve((size_t)batch * kOB * kOB * f);
+  ws.Y = carve((size_t)batch * n * kOB * f);
+  ws.Wf = carve((size_t)batch * nsw * (size_t)nrhs * kOB * f);
+  return ws;
+}
+
+// C[k0:, ccol0 : ccol0 + ncols] of every matrix <- (I - V T^(T) V^T) C over the blocks of
+// reflectors, first to last (Q^T) or last to first (Q). C has row stride ldc and batch stride
+// c_bstride. For sorgqr (first_col_only_from_k0) the block at k0 touches only columns >= k0 of
+// C: the columns left of it are still those of the identity, zero in rows >= k0.
+static cudaError_t apply_q_blocks(const float* H, const float* tau, float* C, long long batch, int n, int ldc,
+                                  long long c_bstride, int ncols, bool transpose_q, bool orgqr,
+                                  const ApplyWorkspace& ws, cudaStream_t s) {
+  cudaError_t e = tc128_configure();
+  if (e != cudaSuccess) return e;
+  const int nblocks = cdiv(n, kOB);
+  for (int bi = 0; bi < nblocks; ++bi) {
+    const int blk = transpose_q ? bi : nblocks - 1 - bi;
+    const int k0 = blk * kOB, ow = std::min(kOB, n - k0), m = n - k0;
+    const int nsw = cdiv(m, kApplyRowsPerSplit);
+    const double bm = (double)batch * m;
+    const int cfirst = orgqr ? k0 : 0;             // first column of C this block changes
+    const int nc = orgqr ? ncols - k0 : ncols;     // columns it changes
+    WyParams g{};
+    g.src = H;
+    g.src_bstride = (long long)n * n;
+    g.H = const_cast<float*>(H);
+    g.Wp = ws.Gp;
+    g.n = n;
+    g.k = k0;
+    g.w = ow;
+    g.cend = n;
+    g.nsplit = nsw;
+    g.rows_per_split = kApplyRowsPerSplit;
+    g.ncmax = kOB;
+    {
+      LaunchScope ls(K_GRAM, 2.0 * bm * ow * ow, 4.0 * bm * ow);
+      tc_vtcw_pipe_kernel<kOB, true, 3><<<dim3(1, nsw, (unsigned)batch), 128, vtcw_pipe_smem<kOB, true, 3>(), s>>>(g);
+    }
+    {
+      LaunchScope ls(K_LARFT, batch * 4.0 * 2.0 * 32 * 32 * 32 / 3.0, 4.0 * batch * (nsw * 4.0 + 4.0) * 32 * 32);
+      larft_blocks_kernel<<<(unsigned)batch, 128, 0, s>>>(ws.Gp, nsw, tau, n, k0, ow, ws.Tp);
+    }
+    {
+      LaunchScope ls(K_TBUILD, batch * 2.0 * ow * ow * ow / 3.0, 4.0 * batch * (nsw + 1.0) * ow * ow);
+      TbuildParams tp{ws.Gp, nsw, ws.Tp, ws.Tob, ow, transpose_q ? 0 : 1};
+      tbuild_kernel<<<(unsigned)batch, 256, kTbuildSmem, s>>>(tp);
+    }
+    Gemm128Params gy{};
+    gy.H = H;
+    gy.T = ws.Tob;
+    gy.Y = ws.Y;
+    gy.y_bstride = (long long)n * kOB;
+    gy.n = n;
+    gy.k = k0;
+    gy.w = ow;
+    {
+      LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
+      tc_gemm128_pipe_kernel<MODE_Y, 3><<<dim3(1, cdiv(m, 128), (unsigned)batch), 128, pipe128_smem<3>(), s>>>(gy);
+    }
+    WyParams wp{};
+    wp.src = C;
+    wp.src_bstride = c_bstride;
+    wp.H = const_cast<float*>(H);
+    wp.Wp = ws.Wf;
+    wp.n = n;
+    wp.k = k0;
+    wp.w = ow;
+    wp.cend = k0 + ow + nc;
+    wp.nsplit = nsw;
+    wp.rows_per_split = kApplyRowsPerSplit;
+    wp.ncmax = ncols;
+    wp.ldc = ldc;
+    wp.ccol = cfirst;
+    {
+      LaunchScope ls(K_VTC128, 2.0 * bm * ow * nc, 4.0 * bm * (ow + nc) + 4.0 * batch * nsw * ow * (double)nc);
+      tc_vtcw_pipe_kernel<kOB, false, 3><<<dim3(cdiv(nc, kTcCols), nsw, (unsigned)batch), 128,
+                                           vtcw_pipe_smem<kOB, false, 3>(), s>>>(wp);
+    }
+    Gemm128Params gu{};
+    gu.H = H;
+    gu.src = C;
+    gu.src_bstride = c_bstride;
+    gu.Hout = C;
+    gu.Y = ws.Y;
+    gu.y_bstride = (long long)n * kOB;
+    gu.Wp = ws.Wf;
+    gu.nsplit = nsw;
+    gu.ncmax = ncols;
+    gu.n = n;
+    gu.k = k0;
+    gu.w = ow;
+    gu.cend = k0 + ow + nc;
+    gu.coff = 0;
+    gu.ldc = ldc;
+    gu.ccol = cfirst;
+    gu.hout_bstride = c_bstride;
+    {
+      LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
+      tc_gemm128_pipe_kernel<MODE_UPD, 3><<<dim3(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch), 128, pipe128_smem<3>(),
+                                            s>>>(gu);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Shared argument checks of the two apply entries (QRB200_OK or the status to return).
+static int apply_args_ok(const float* H, const float* tau, const float* C, int64_t batch, int64_t n, int64_t nrhs) {
+  if (batch < 0 || n < 0 || nrhs < 0) return QRB200_ERR_ARG;
+  if (batch == 0 || n == 0 || nrhs == 0) return QRB200_OK;
+  if (n > kMaxN || batch > 65535 || nrhs > (1 << 20)) return QRB200_ERR_ARG;
+  if ((n % 4) != 0 || (nrhs % 4) != 0) return QRB200_ERR_ARG;
+  if (!H || !tau || !C) return QRB200_ERR_ARG;
+  if (((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(C)) & 15u) != 0) return QRB200_ERR_ARG;
+  return QRB200_OK;
+}
+
+// One warp waits, with a short poll limit, on an mbarrier that nothing arrives on: the wait
+// runs out and reports kSiteSelfTest through the same path as the factorisation kernels'
+// waits. Nothing is in flight when it gives up (no copy, no MMA), so the kernel just returns.
+__global__ void selftest_wait_kernel(uint32_t polls) {
+  __shared__ uint64_t mbar;
+  if (threadIdx.x == 0) mbar_init(&mbar, 1);
+  __syncthreads();
+  const bool done = mbar_wait_limit(&mbar, 0, polls, kSiteSelfTest);
+  (void)done;
 }
 
 }  // namespace qrb200
@@ -1279,7 +1057,62 @@ int qrb200_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch
                     stream);
 }
 
+size_t qrb200_apply_workspace_bytes(int64_t batch, int64_t n, int64_t nrhs) {
+  if (batch <= 0 || n <= 0 || nrhs <= 0 || n > kMaxN || nrhs > (1 << 20)) return 0;
+  return apply_layout(batch, (int)n, (int)nrhs, nullptr).bytes;
+}
+
+int qrb200_ormqr_f32(const float* H, const float* tau, float* C, int64_t batch, int64_t n, int64_t nrhs,
+                     int transpose, void* workspace, size_t workspace_bytes, void* stream) {
+  const int a = apply_args_ok(H, tau, C, batch, n, nrhs);
+  if (a != QRB200_OK || batch == 0 || n == 0 || nrhs == 0) return a;
+  const int dev_ok = check_device();
+  if (dev_ok != QRB200_OK) return dev_ok;
+  const ApplyWorkspace ws = apply_layout(batch, (int)n, (int)nrhs, workspace);
+  if (!workspace || workspace_bytes < ws.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return QRB200_ERR_WORKSPACE;
+  const cudaError_t e = apply_q_blocks(H, tau, C, batch, (int)n, (int)nrhs, n * nrhs, (int)nrhs, transpose != 0,
+                                       false, ws, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
+}
+
+int qrb200_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int64_t n, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  const int a = apply_args_ok(H, tau, Q, batch, n, n);
+  if (a != QRB200_OK || batch == 0 || n == 0) return a;
+  const int dev_ok = check_device();
+  if (dev_ok != QRB200_OK) return dev_ok;
+  const ApplyWorkspace ws = apply_layout(batch, (int)n, (int)n, workspace);
+  if (!workspace || workspace_bytes < ws.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return QRB200_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    const long long quads = batch * n * n / 4;
+    const int grid = (int)std::min<long long>(cdiv(quads, 256), 16LL * num_sms());
+    LaunchScope ls(K_FILL, 0.0, 4.0 * batch * n * (double)n);
+    set_identity_kernel<<<grid, 256, 0, s>>>(Q, batch, (int)n);
+  }
+  if (cudaGetLastError() != cudaSuccess) return QRB200_ERR_CUDA;
+  const cudaError_t e = apply_q_blocks(H, tau, Q, batch, (int)n, (int)n, n * n, (int)n, false, true, ws, s);
+  return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
+}
+
 long long qrb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int qrb200_diag_wide_update_f32(float* H, const float* Y, int64_t batch, int64_t n, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (batch <= 0 || n <= kOB || n > 1024 || (n % 4) != 0 || batch > 65535 || !H || !Y) return QRB200_ERR_ARG;
+  if (((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(Y)) & 15u) != 0) return QRB200_ERR_ARG;
+  const int dev_ok = check_device();
+  if (dev_ok != QRB200_OK) return dev_ok;
+  const Workspace ws = layout(batch, (int)n, workspace);
+  if (!workspace || workspace_bytes < ws.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return QRB200_ERR_WORKSPACE;
+  if (tc128_configure() != cudaSuccess) return QRB200_ERR_CUDA;
+  const cudaError_t e = launch_wide(H, (long long)n * n, H, Y, ws, batch, (int)n, 0, kOB, 0, (int)n,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
+}
 
 int qrb200_profile_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int64_t n,
                              int64_t a_batch_stride, void* workspace, size_t workspace_bytes,
@@ -1334,7 +1167,7 @@ static int geqrf_impl(const float* A, float* H, float* tau, int64_t batch, int64
     const Workspace ws = layout(batch, (int)n, workspace);
     if (workspace_bytes < ws.bytes || !workspace) return QRB200_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return QRB200_ERR_WORKSPACE;
-    if (use_single_la((int)n) && !use_tc_update((int)n, A, a_batch_stride))
+    if (use_single_la((int)n))
       e = run_single_la(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
     else if (use_two_level((int)n, A, a_batch_stride))
       e = run_two_level(A, H, tau, batch, (int)n, a_batch_stride, ws, s);
@@ -1370,8 +1203,36 @@ int qrb200_device_status(int* status_out) {
   if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return QRB200_ERR_CUDA;
   const int zero = 0;
   if (v != 0 && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return QRB200_ERR_CUDA;
-  *status_out = v;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kStatusWords) {
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    if (g_status_host) reinterpret_cast<volatile int*>(g_status_host)[dev] = 0;
+  }
+  *status_out = v != 0 ? QRB200_ERR_TIMEOUT : QRB200_OK;
   return QRB200_OK;
+}
+
+int qrb200_last_status(int* site_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QRB200_ERR_CUDA;
+  int v = 0;
+  if (dev >= 0 && dev < kStatusWords) {
+    std::lock_guard<std::mutex> lk(g_status_mu);
+    if (g_status_host) {
+      volatile int* w = reinterpret_cast<volatile int*>(g_status_host) + dev;
+      v = *w;
+      if (v != 0) *w = 0;
+    }
+  }
+  if (site_out) *site_out = v;
+  return v != 0 ? QRB200_ERR_TIMEOUT : QRB200_OK;
+}
+
+int qrb200_selftest_wait_timeout(uint32_t polls, void* stream) {
+  const int dev_ok = check_device();
+  if (dev_ok != QRB200_OK) return dev_ok;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(polls);
+  return cudaGetLastError() == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
 }
 
 }  // extern "C"

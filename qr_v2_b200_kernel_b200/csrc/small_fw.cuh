@@ -26,8 +26,6 @@
 
 namespace qrb200 {
 
-constexpr int kDevStatusHandoffTimeout = 6;
-
 __device__ __forceinline__ int ld_acquire_cta(const int* p) {
   int v;
   asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
@@ -41,7 +39,7 @@ __device__ __forceinline__ void st_release_cta(int* p, int v) {
 __device__ __forceinline__ bool fw_wait_geq(const int* p, int v) {
   for (uint32_t it = 0; it < (1u << 24); ++it)
     if (ld_acquire_cta(p) >= v) return true;
-  atomicExch(&g_device_status, kDevStatusHandoffTimeout);
+  report_device_failure(kSiteHandoff);
   return false;
 }
 
@@ -52,7 +50,7 @@ __device__ __forceinline__ bool fw_wait_geq_sleep(const int* p, int v) {
     if (ld_acquire_cta(p) >= v) return true;
     __nanosleep(100);
   }
-  atomicExch(&g_device_status, kDevStatusHandoffTimeout);
+  report_device_failure(kSiteHandoff);
   return false;
 }
 
@@ -63,7 +61,7 @@ __device__ __forceinline__ bool fw_wait_geq_pause(const int* p, int v, int ns) {
     if (ld_acquire_cta(p) >= v) return true;
     __nanosleep(ns);
   }
-  atomicExch(&g_device_status, kDevStatusHandoffTimeout);
+  report_device_failure(kSiteHandoff);
   return false;
 }
 

@@ -32,12 +32,37 @@
 
 namespace qrb200 {
 
-// Device status word read by qrb200_device_status (0 = no failure) and its failure codes.
-constexpr int kDevStatusMmaTimeout = 5;
+// Device-side failure reporting. A kernel whose bounded wait expires records the site of the
+// wait (a code below, never 0) in g_device_status (device memory, read by the synchronous
+// qrb200_device_status) and, once the host has registered it, in this device's word of a
+// mapped pinned host array (g_status_mapped), which qrb200_last_status and the Python operator
+// read without any CUDA call or synchronisation.
+constexpr int kSiteMbarrier = 1;    // mbarrier wait of a tensor-core kernel (MMA or operand ring)
+constexpr int kSiteHandoff = 2;     // hand-off flag of the whole-matrix kernel
+constexpr int kSiteCluster = 3;     // partial-sum exchange of the cluster panel
+constexpr int kSiteSelfTest = 4;    // qrb200_selftest_wait_timeout
 __device__ int g_device_status = 0;
+__device__ int* g_status_mapped = nullptr;
+
+__device__ __noinline__ void report_device_failure(int site) {
+  atomicExch(&g_device_status, site);
+  int* h = g_status_mapped;
+  if (h != nullptr) {
+    *reinterpret_cast<volatile int*>(h) = site;
+    __threadfence_system();
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+constexpr int kTcCols = 128;  // trailing columns per CTA of the V^T C products (MMA M)
+
+// First 1024-byte aligned address at or after p in shared memory (swizzled operand tiles).
+__device__ __forceinline__ unsigned char* align1024(unsigned char* p) {
+  const uint32_t s = smem_u32(p);
+  return p + ((1024u - (s & 1023u)) & 1023u);
 }
 
 // cp.async: a 16-byte (or 4-byte) global -> shared copy that bypasses registers; an invalid
@@ -140,11 +165,11 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" : : "r"(smem_u32(mbar)), "r"(count) : "memory");
 }
 
-// Bounded wait for phase `parity` of an mbarrier. Returns false (and records the failure in
-// the device status word) if the phase did not complete within the iteration limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
+// Bounded wait for phase `parity` of an mbarrier: false (and the failure recorded at `site`)
+// if the phase did not complete within `limit` polls.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* mbar, uint32_t parity, uint32_t limit, int site) {
   const uint32_t addr = smem_u32(mbar);
-  for (uint32_t it = 0; it < (1u << 24); ++it) {
+  for (uint32_t it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -155,8 +180,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
         : "memory");
     if (done) return true;
   }
-  atomicExch(&g_device_status, kDevStatusMmaTimeout);
+  report_device_failure(site);
   return false;
+}
+
+// The tensor-core kernels' wait: 2^24 polls (on the order of a second).
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity) {
+  return mbar_wait_limit(mbar, parity, 1u << 24, kSiteMbarrier);
 }
 
 __device__ __forceinline__ void fence_async_smem() {

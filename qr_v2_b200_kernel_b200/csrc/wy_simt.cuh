@@ -30,6 +30,9 @@ struct WyParams {
   int ncmax;              // leading dimension of Wp / W2 (>= cend - k - w)
   int coff;               // first trailing column (relative to k + w) of this launch (tile-aligned
                           // for the 128-wide kernels)
+  // C outside H (tc_vtcw_pipe_kernel only): row stride of src and the column of src that holds
+  // trailing column 0. ldc == 0: C is in the matrix itself (row stride n, column k + w).
+  int ldc, ccol;
 };
 
 // V[r][c] of the panel starting at (k, k): unit lower trapezoid stored in H.

@@ -5,11 +5,11 @@
 //   wy_vtc2_kernel : Wp[s] = V_s^T C_s  over a row split s; 32 x 128 outputs per CTA, the rows
 //                    streamed in 32-row stages by cp.async (three stages in flight), 4 x 4
 //                    outputs per thread;
-//   wy_upd2_kernel : C <- C - V W2 on a 128 x 64 tile, K = 32: V (transposed) and W2 staged in
-//                    shared memory while each thread's 8 x 4 slice of C is already on its way
-//                    into registers.
-// The T^T product between them is wy_tw_kernel. Same arithmetic per output as wy_simt.cuh
-// except for the summation order inside each partial product.
+//   wy_vtcn_kernel : the same for updates of 32 or 64 columns;
+//   wy_tw2_kernel  : W2 = T^T sum_s Wp[s];
+//   wy_upd3_kernel / wy_upd4_kernel : C <- C - V W2 over persistent tiles, cp.async rings.
+// Same arithmetic per output as wy_simt.cuh except for the summation order inside each
+// partial product.
 #pragma once
 
 #include "common.cuh"
@@ -100,175 +100,6 @@ __global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
     for (int i = 0; i < 4; ++i)
       *reinterpret_cast<float4*>(out + (long long)(4 * ty + i) * P.ncmax + col) =
           make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-  }
-}
-
-constexpr int kU2Rows = 128, kU2Cols = 64;
-struct Upd2Shared {
-  float Vt[32][kU2Rows + 4];  // V transposed: Vt[c][r]
-  float W[32][kU2Cols];
-};
-
-__global__ void __launch_bounds__(256) wy_upd2_kernel(WyParams P) {
-  __shared__ __align__(16) Upd2Shared sh;
-  const int bidx = blockIdx.z;
-  const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
-  const int row0 = blockIdx.y * kU2Rows, col0 = P.coff + blockIdx.x * kU2Cols;
-  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
-  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
-  float* __restrict__ Ho = P.H + (long long)bidx * n * n;
-  const float* __restrict__ W2b = P.W2 + (long long)bidx * 32 * P.ncmax;
-  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int col = col0 + 4 * tx;
-  const bool col_ok = col < nc;
-  // This thread's C slice (rows row0 + 8 ty .. +7, columns col .. col+3), requested first.
-  float4 cv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = row0 + 8 * ty + i;
-    cv[i] = (r < m && col_ok) ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + col)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  // V tile (128 x 32, masked unit lower trapezoid) transposed into shared memory.
-#pragma unroll
-  for (int it = 0; it < 4; ++it) {
-    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = row0 + rr, c = 4 * q;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < m && c < w) v = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
-    float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e2 = 0; e2 < 4; ++e2) vv[e2] = (c + e2 >= w) ? 0.f : (r > c + e2 ? vv[e2] : (r == c + e2 ? 1.f : 0.f));
-#pragma unroll
-    for (int e2 = 0; e2 < 4; ++e2) sh.Vt[c + e2][rr] = vv[e2];
-  }
-#pragma unroll
-  for (int it = 0; it < 2; ++it) {
-    const int e = it * 256 + tid, c = e >> 4, q = e & 15, cl = col0 + 4 * q;
-    *reinterpret_cast<float4*>(&sh.W[c][4 * q]) =
-        (cl < nc) ? *reinterpret_cast<const float4*>(W2b + (long long)c * P.ncmax + cl) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  __syncthreads();
-  float acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
-#pragma unroll 8
-  for (int c = 0; c < 32; ++c) {
-    const float4 v0 = *reinterpret_cast<const float4*>(&sh.Vt[c][8 * ty]);
-    const float4 v1 = *reinterpret_cast<const float4*>(&sh.Vt[c][8 * ty + 4]);
-    const float4 x = *reinterpret_cast<const float4*>(&sh.W[c][4 * tx]);
-    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w}, xx[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], xx[e], acc[i][e]);
-  }
-  if (!col_ok) return;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = row0 + 8 * ty + i;
-    if (r < m)
-      *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
-          make_float4(cv[i].x - acc[i][0], cv[i].y - acc[i][1], cv[i].z - acc[i][2], cv[i].w - acc[i][3]);
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// Wide-tile V^T C: 32 x 256 outputs per CTA (8 x 4 per thread: the eight V columns of a warp
-// are one broadcast read, the four C columns one conflict-free float4), rows streamed in
-// 16-row stages, four stages in flight.
-constexpr int kV3Cols = 256, kV3Rows = 16, kV3Stages = 4;
-struct Vtc3Stage {
-  float C[kV3Rows][kV3Cols];
-  float V[kV3Rows][32];
-};
-constexpr size_t kVtc3Smem = sizeof(Vtc3Stage) * kV3Stages;
-
-__global__ void __launch_bounds__(256) wy_vtc3_kernel(WyParams P) {
-  griddep_launch_wait();
-  extern __shared__ __align__(16) unsigned char v3_smem_raw[];
-  Vtc3Stage* st = reinterpret_cast<Vtc3Stage*>(v3_smem_raw);
-  const int bidx = blockIdx.z, split = blockIdx.y;
-  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
-  const int col0 = P.coff + blockIdx.x * kV3Cols;
-  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
-  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
-  const int tid = threadIdx.x, cg = tid & 63, rg = tid >> 6;
-  const int r_begin = split * P.rows_per_split;
-  const int r_end = min(n - k, r_begin + P.rows_per_split);
-  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV3Rows - 1) / kV3Rows : 0;
-
-  auto issue = [&](int ch) {
-    Vtc3Stage& s = st[ch % kV3Stages];
-    const int rb = r_begin + ch * kV3Rows;
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {  // C: 16 rows x 64 float4
-      const int e = it * 256 + tid, rr = e >> 6, q = e & 63, r = rb + rr, col = col0 + 4 * q;
-      const bool ok = r < r_end && col < nc;
-      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
-    }
-    if (tid < 128) {  // V: 16 rows x 8 float4
-      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
-      const bool ok = r < r_end && 4 * q < w;
-      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
-    }
-  };
-
-  // acc[ip][e] holds W rows 8 rg + 2 ip and 8 rg + 2 ip + 1 of column 4 cg + e (paired FMAs).
-  float2 acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int s = 0; s < kV3Stages - 1; ++s) {
-    if (s < nchunks) issue(s);
-    cp_async_commit();
-  }
-  for (int ch = 0; ch < nchunks; ++ch) {
-    cp_async_wait<kV3Stages - 2>();
-    __syncthreads();
-    if (ch + kV3Stages - 1 < nchunks) issue(ch + kV3Stages - 1);
-    cp_async_commit();
-    Vtc3Stage& s = st[ch % kV3Stages];
-    if (split == 0 && ch < 2) {
-      // Panel rows 0..31 (the first two stages): V is unit lower triangular there.
-#pragma unroll
-      for (int it = 0; it < 2; ++it) {
-        const int e = it * 256 + tid, rr = e >> 5, c = e & 31, r = ch * kV3Rows + rr;
-        const float v = s.V[rr][c];
-        s.V[rr][c] = (c >= w) ? 0.f : (r > c ? v : (r == c ? 1.f : 0.f));
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int rr = 0; rr < kV3Rows; ++rr) {
-      const float4 v0 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg]);
-      const float4 v1 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg + 4]);
-      const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * cg]);
-      const float2 vp[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w), make_float2(v1.x, v1.y),
-                            make_float2(v1.z, v1.w)};
-      const float cc[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 ce = make_float2(cc[e], cc[e]);
-#pragma unroll
-        for (int ip = 0; ip < 4; ++ip) acc[ip][e] = __ffma2_rn(vp[ip], ce, acc[ip][e]);
-      }
-    }
-  }
-  cp_async_wait<0>();
-  const int col = col0 + 4 * cg;
-  if (col < nc) {
-    float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
-#pragma unroll
-    for (int ip = 0; ip < 4; ++ip) {
-      *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip) * P.ncmax + col) =
-          make_float4(acc[ip][0].x, acc[ip][1].x, acc[ip][2].x, acc[ip][3].x);
-      *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip + 1) * P.ncmax + col) =
-          make_float4(acc[ip][0].y, acc[ip][1].y, acc[ip][2].y, acc[ip][3].y);
-    }
   }
 }
 
@@ -555,102 +386,6 @@ __global__ void __launch_bounds__(256) wy_tw2_kernel(WyParams P) {
     float acc = 0.f;
     for (int cc = 0; cc <= i; ++cc) acc = fmaf(Ts[cc][i], Ws[cc][c], acc);
     out[(long long)i * P.ncmax + col] = acc;
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// V^T C with 8 x 8 outputs per thread (128 threads, 32 x 256 outputs per CTA): per row, two
-// broadcast float4 reads of V and two contiguous float4 reads of C (columns 4 cg .. and
-// 128 + 4 cg ..) feed 64 FMAs, so shared memory is no longer the limiter. Same stages as
-// wy_vtc3_kernel.
-__global__ void __launch_bounds__(128) wy_vtc4_kernel(WyParams P) {
-  extern __shared__ __align__(16) unsigned char v4_smem_raw[];
-  Vtc3Stage* st = reinterpret_cast<Vtc3Stage*>(v4_smem_raw);
-  const int bidx = blockIdx.z, split = blockIdx.y;
-  const int n = P.n, k = P.k, w = P.w, nc = P.cend - k - w;
-  const int col0 = P.coff + blockIdx.x * kV3Cols;
-  const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
-  const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
-  const int tid = threadIdx.x, cg = tid & 31, rg = tid >> 5;
-  const int r_begin = split * P.rows_per_split;
-  const int r_end = min(n - k, r_begin + P.rows_per_split);
-  const int nchunks = r_end > r_begin ? (r_end - r_begin + kV3Rows - 1) / kV3Rows : 0;
-
-  auto issue = [&](int ch) {
-    Vtc3Stage& s = st[ch % kV3Stages];
-    const int rb = r_begin + ch * kV3Rows;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {  // C: 16 rows x 64 float4
-      const int e = it * 128 + tid, rr = e >> 6, q = e & 63, r = rb + rr, col = col0 + 4 * q;
-      const bool ok = r < r_end && col < nc;
-      cp_async16(&s.C[rr][4 * q], ok ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok);
-    }
-    {  // V: 16 rows x 8 float4
-      const int rr = tid >> 3, q = tid & 7, r = rb + rr;
-      const bool ok = r < r_end && 4 * q < w;
-      cp_async16(&s.V[rr][4 * q], ok ? Hb + (long long)(k + r) * n + k + 4 * q : Hb, ok);
-    }
-  };
-
-  // acc[ip][e]: W rows 8 rg + 2 ip, + 1 of column e of this thread's eight
-  // (e < 4: 4 cg + e; e >= 4: 128 + 4 cg + e - 4).
-  float2 acc[4][8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[i][e] = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int s = 0; s < kV3Stages - 1; ++s) {
-    if (s < nchunks) issue(s);
-    cp_async_commit();
-  }
-  for (int ch = 0; ch < nchunks; ++ch) {
-    cp_async_wait<kV3Stages - 2>();
-    __syncthreads();
-    if (ch + kV3Stages - 1 < nchunks) issue(ch + kV3Stages - 1);
-    cp_async_commit();
-    Vtc3Stage& s = st[ch % kV3Stages];
-    if (split == 0 && ch < 2) {
-      // Panel rows 0..31 (the first two stages): V is unit lower triangular there.
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int e = it * 128 + tid, rr = e >> 5, c = e & 31, r = ch * kV3Rows + rr;
-        const float v = s.V[rr][c];
-        s.V[rr][c] = (c >= w) ? 0.f : (r > c ? v : (r == c ? 1.f : 0.f));
-      }
-      __syncthreads();
-    }
-#pragma unroll 4
-    for (int rr = 0; rr < kV3Rows; ++rr) {
-      const float4 v0 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg]);
-      const float4 v1 = *reinterpret_cast<const float4*>(&s.V[rr][8 * rg + 4]);
-      const float4 c0 = *reinterpret_cast<const float4*>(&s.C[rr][4 * cg]);
-      const float4 c1 = *reinterpret_cast<const float4*>(&s.C[rr][128 + 4 * cg]);
-      const float2 vp[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w), make_float2(v1.x, v1.y),
-                            make_float2(v1.z, v1.w)};
-      const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float2 ce = make_float2(cc[e], cc[e]);
-#pragma unroll
-        for (int ip = 0; ip < 4; ++ip) acc[ip][e] = __ffma2_rn(vp[ip], ce, acc[ip][e]);
-      }
-    }
-  }
-  cp_async_wait<0>();
-  float* out = P.Wp + ((long long)bidx * P.nsplit + split) * 32 * P.ncmax;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int col = col0 + 128 * h + 4 * cg;
-    if (col < nc) {
-#pragma unroll
-      for (int ip = 0; ip < 4; ++ip) {
-        *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip) * P.ncmax + col) =
-            make_float4(acc[ip][4 * h].x, acc[ip][4 * h + 1].x, acc[ip][4 * h + 2].x, acc[ip][4 * h + 3].x);
-        *reinterpret_cast<float4*>(out + (long long)(8 * rg + 2 * ip + 1) * P.ncmax + col) =
-            make_float4(acc[ip][4 * h].y, acc[ip][4 * h + 1].y, acc[ip][4 * h + 2].y, acc[ip][4 * h + 3].y);
-      }
-    }
   }
 }
 

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const int n = P.n, k = P.k, w = P.w, m = n - k;
   const int ncols = (MODE == MODE_Y) ? kOB : P.cend - k - w;
   const int col0 = (MODE == MODE_UPD ? P.coff : 0) + blockIdx.x * 128, row0 = blockIdx.y * 128;
+  const int ldc = P.ldc > 0 ? P.ldc : n, ccol = P.ldc > 0 ? P.ccol : k + w;
+  const long long hob = P.ldc > 0 ? P.hout_bstride : (long long)n * n;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
   const float* __restrict__ Bsrc = (MODE == MODE_Y) ? P.T + (long long)bidx * kOB * kOB
@@ -57,7 +59,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   if (MODE == MODE_UPD && row0 + tid < m) {
     // The epilogue's slice of C (this thread's row, 128 columns) starts moving HBM -> L2 now,
     // under the K loop, instead of after it.
-    const float* crow = P.src + (long long)bidx * P.src_bstride + (long long)(k + row0 + tid) * n + k + w + col0;
+    const float* crow = P.src + (long long)bidx * P.src_bstride + (long long)(k + row0 + tid) * ldc + ccol + col0;
     const int last = min(ncols - col0, 128) - 1;
     if (last >= 0) {
 #pragma unroll
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   // 32 partial ones. The next chunk's C is in flight while the current one is processed.
   const int lane = tid & 31, lr = lane >> 3, lq = lane & 7;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
-  float* __restrict__ Ho = P.Hout + (long long)bidx * n * n;
+  float* __restrict__ Ho = P.Hout + (long long)bidx * hob;
   constexpr int kPad = 36;  // row stride of the staging tile (floats): conflict-free float4 rows
   float* stg = reinterpret_cast<float*>(&sh.st[0]) + warp * (32 * kPad);
   auto load_chunk = [&](int q, float4 (&cv)[8]) {
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
     for (int i = 0; i < 8; ++i) {
       const int r = row0 + 32 * warp + 4 * i + lr;
       cv[i] = (MODE == MODE_UPD && r < m && c < ncols)
-                  ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + c)
+                  ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * ldc + ccol + c)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
       if (MODE == MODE_Y) {
         *reinterpret_cast<float4*>(P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + c) = p;
       } else {
-        *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + c) =
+        *reinterpret_cast<float4*>(Ho + (long long)(k + r) * ldc + ccol + c) =
             make_float4(cur[i].x - p.x, cur[i].y - p.y, cur[i].z - p.z, cur[i].w - p.w);
       }
     }
@@ -258,6 +260,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
   const int n = P.n, k = P.k, w = P.w, m = n - k;
   const int nc = GRAM ? w : P.cend - k - w;
   const int col0 = (GRAM ? 0 : P.coff) + blockIdx.x * kTcCols;
+  const int ldc = P.ldc > 0 ? P.ldc : n, ccol = P.ldc > 0 ? P.ccol : k + w;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   const int r_begin = split * P.rows_per_split;
@@ -305,7 +308,7 @@ __global__ void __launch_bounds__(128) tc_vtcw_pipe_kernel(WyParams P) {
       const int r = r0 + kk, col = col0 + mn;
       const bool ok_c = r < r_end && col < nc;
       cp_async16(st.c_hi + (sw32_off(mn, kk, LBO, SBO_C) >> 2),
-                 ok_c ? Sb + (long long)(k + r) * n + k + w + col : Sb, ok_c);
+                 ok_c ? Sb + (long long)(k + r) * ldc + ccol + col : Sb, ok_c);
     }
   };
   auto split_inplace = [](float* hi, float* lo, uint32_t off) {

@@ -21,7 +21,7 @@ def kernel_breakdown(A: torch.Tensor, steps: int = 1) -> list[dict]:
     H = torch.empty_like(A)
     tau = torch.empty((batch, n), dtype=torch.float32, device=A.device)
     stream = torch.cuda.current_stream(A.device).cuda_stream
-    ws = _workspace(A.device, stream, workspace_bytes(batch, n))
+    ws = _workspace(A.device, workspace_bytes(batch, n))
     agg: dict[str, dict] = {}
     for _ in range(steps):
         stats = (_lib.KernelStat * 16)()

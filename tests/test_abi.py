@@ -110,3 +110,44 @@ def test_host_api_rejects_bad_inputs_on_cpu():
     assert _host_chunks(8, 2048) == 2 and _host_chunks(2, 4096) == 2  # C4, C5: 134 MB
     assert _host_chunks(64, 1024) == 4 and _host_chunks(640, 512) == 4  # C3, C2
     assert _host_chunks(1, 4096) == 1  # never more pieces than matrices
+
+
+def test_geqrf_rejects_bad_operands_on_cpu():
+    import torch
+
+    from qr_v2_b200_kernel_b200 import geqrf
+
+    A = torch.zeros(2, 4, 4)
+    with pytest.raises(TypeError):
+        geqrf([[1.0]], A, torch.zeros(2, 4))
+    with pytest.raises(TypeError):
+        geqrf(A.double(), A, torch.zeros(2, 4))
+    with pytest.raises(RuntimeError):
+        geqrf(A, A.clone(), torch.zeros(2, 4))  # host tensors: no CPU path
+
+
+def test_status_entries_without_a_device(lib):
+    # No CUDA device here: the status read fails with a CUDA error instead of touching memory.
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("needs a host without a GPU")
+    assert lib.qrb200_last_status(None) == _lib.QRB200_ERR_CUDA
+
+
+def test_apply_entries_host_checks(lib):
+    p = ctypes.c_void_p(16)
+    assert lib.qrb200_apply_workspace_bytes(2, 512, 64) > 0
+    assert lib.qrb200_apply_workspace_bytes(2, 512, 64) % 256 == 0
+    assert lib.qrb200_apply_workspace_bytes(0, 512, 64) == 0
+    assert lib.qrb200_apply_workspace_bytes(1, 8192, 8) == 0  # unsupported order
+    f = lib.qrb200_ormqr_f32
+    assert f(p, p, p, 1, 30, 8, 1, None, 0, None) == _lib.QRB200_ERR_ARG  # n % 4 != 0
+    assert f(p, p, p, 1, 32, 6, 1, None, 0, None) == _lib.QRB200_ERR_ARG  # nrhs % 4 != 0
+    assert f(None, p, p, 1, 32, 8, 0, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert f(ctypes.c_void_p(20), p, p, 1, 32, 8, 0, None, 0, None) == _lib.QRB200_ERR_ARG  # unaligned H
+    assert f(p, p, p, 0, 32, 8, 1, None, 0, None) == _lib.QRB200_OK  # empty batch: no-op
+    g = lib.qrb200_orgqr_f32
+    assert g(p, p, p, 1, 5000, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert g(p, p, p, -1, 32, None, 0, None) == _lib.QRB200_ERR_ARG
+    assert g(p, p, p, 3, 0, None, 0, None) == _lib.QRB200_OK
