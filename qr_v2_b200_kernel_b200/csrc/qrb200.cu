@@ -21,7 +21,7 @@
 #include <mutex>
 #include <vector>
 
-#include "../../include/qrb200.h"
+#include "qrb200.h"
 #include "panel.cuh"
 #include "panel_fw.cuh"
 #include "panel_cl.cuh"
@@ -513,7 +513,7 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     }
     const int cp = cdiv(m, kU1Rows);
     LaunchScope ls(K_U1, 4.0 * bm * w * ncl + (double)batch * w * w * ncl, 12.0 * bm * ncl + 4.0 * bm * w);
-    return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(256), kU1Smem, s,
+    return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(kU1Threads), kU1Smem, s,
                     (unsigned)cp, true, wp);
   }
   const bool vtc_tc = vec && ncl > kV2Cols;  // wide V^T C on tcgen05, partials stored transposed

@@ -3,15 +3,18 @@
 // updates that sit on the critical path: the next panel's columns under look-ahead, or the
 // narrow updates inside an outer block. Rows must start on 16-byte boundaries.
 //
-// A thread-block cluster of CP CTAs covers the m rows (256 per CTA); blockIdx.y picks a
-// 32-column slice of C, blockIdx.z the matrix. Each CTA
+// A thread-block cluster of CP CTAs covers the m rows (256 per CTA, 512 threads: the few CTAs of
+// this critical-path launch have their SMs to themselves, so every phase is spread over twice
+// the threads of a resident-CTA design); blockIdx.y picks a 32-column slice of C, blockIdx.z the
+// matrix. Each CTA
 //   (1) stages its rows of V (unit lower trapezoid, masked) and of the C slice in shared memory
 //       with coalesced 16-byte loads,
-//   (2) forms its partial W_p = V_p^T C_p (32 x 32; each thread a 4 x 4 block over a quarter
-//       of the rows, the quarters added in shared memory),
+//   (2) forms its partial W_p = V_p^T C_p (32 x 32; each thread a 4 x 4 block over an eighth of
+//       the rows, the eighths added in shared memory in a fixed order),
 //   (3) after one cluster barrier adds the CP partials from the peers' shared memory in rank
-//       order (every CTA gets bitwise the same W) and forms W2 = T^T W,
-//   (4) writes C_p - V_p W2 back (one row per thread, stored through shared memory).
+//       order (two halves of the peers read by two thread halves, then added: every CTA gets
+//       bitwise the same W) and forms W2 = T^T W,
+//   (4) writes C_p - V_p W2 back (two threads per row, 16 columns each, through shared memory).
 // A second cluster barrier keeps every CTA's partial readable until all peers are done.
 #pragma once
 
@@ -22,13 +25,14 @@
 
 namespace qrb200 {
 
-constexpr int kU1Rows = 256, kU1Ld = 36;
+constexpr int kU1Rows = 256, kU1Ld = 36, kU1Threads = 512;
 
 struct __align__(16) U1Shared {
   float V[kU1Rows][kU1Ld];
   float C[kU1Rows][kU1Ld];
-  float Wq[4][32][32];  // row-quarter partials
+  float Wq[8][32][32];  // row-eighth partials
   float W[32][32];      // this CTA's partial V^T C, read by the peers
+  float Wh[32][32];     // sum of the upper half of the peers' partials
   float Wt[32][33];     // the cluster total
   float W2[32][32];     // T^T W
   float T[32][33];
@@ -43,7 +47,7 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   return x;
 }
 
-__global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
+__global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
   griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char u1_smem_raw[];
   U1Shared& sh = *reinterpret_cast<U1Shared*>(u1_smem_raw);
@@ -59,14 +63,14 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Ho = P.H + (long long)bidx * n * n;
 
-  // (1) stage V, C and T (8 threads per row, 16 bytes each); T's four loads per thread are
+  // (1) stage V, C and T (8 threads per row, 16 bytes each); T's two loads per thread are
   // issued first, so every load of the stage is in flight together.
-  float tv[4];
+  float tv[2];
 #pragma unroll
-  for (int it = 0; it < 4; ++it) tv[it] = P.T[(long long)bidx * P.t_bstride + it * 256 + tid];
+  for (int it = 0; it < 2; ++it) tv[it] = P.T[(long long)bidx * P.t_bstride + it * kU1Threads + tid];
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
+  for (int it = 0; it < 4; ++it) {
+    const int e = it * kU1Threads + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f), x = v;
     if (r < m) {
       if (c < w) v = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
@@ -82,12 +86,12 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
     *reinterpret_cast<float4*>(&sh.C[rr][c]) = x;
   }
 #pragma unroll
-  for (int it = 0; it < 4; ++it) {
-    const int e = it * 256 + tid;
+  for (int it = 0; it < 2; ++it) {
+    const int e = it * kU1Threads + tid;
     sh.T[e >> 5][e & 31] = tv[it];
   }
   __syncthreads();
-  // (2) partial W over the slab: thread (rq, ig, cg) sums rows rq, rq + 4, ... for a 4 x 4 block.
+  // (2) partial W over the slab: thread (rq, ig, cg) sums rows rq, rq + 8, ... for a 4 x 4 block.
   {
     const int cg = tid & 7, ig = (tid >> 3) & 7, rq = tid >> 6;
     float acc[4][4];
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
 #pragma unroll
       for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
 #pragma unroll 4
-    for (int r = rq; r < kU1Rows; r += 4) {
+    for (int r = rq; r < kU1Rows; r += 8) {
       const float4 v = *reinterpret_cast<const float4*>(&sh.V[r][4 * ig]);
       const float4 x = *reinterpret_cast<const float4*>(&sh.C[r][4 * cg]);
       const float vv[4] = {v.x, v.y, v.z, v.w}, xx[4] = {x.x, x.y, x.z, x.w};
@@ -110,11 +114,11 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
       *reinterpret_cast<float4*>(&sh.Wq[rq][4 * ig + a][4 * cg]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
   }
   __syncthreads();
-  const int i = tid >> 3, cq = tid & 7;
-  {
+  const int i = (tid >> 3) & 31, cq = tid & 7, half = tid >> 8;
+  if (half == 0) {
     float4 s = *reinterpret_cast<const float4*>(&sh.Wq[0][i][4 * cq]);
 #pragma unroll
-    for (int q = 1; q < 4; ++q) {
+    for (int q = 1; q < 8; ++q) {
       const float4 t = *reinterpret_cast<const float4*>(&sh.Wq[q][i][4 * cq]);
       s.x += t.x;
       s.y += t.y;
@@ -123,28 +127,37 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
     }
     *reinterpret_cast<float4*>(&sh.W[i][4 * cq]) = s;
   }
-  // (3) cluster total in rank order, then W2 = T^T W.
+  // (3) cluster total in rank order (peers 0..7 by the lower thread half, 8..15 by the upper
+  // half, then the two half sums added), then W2 = T^T W.
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   {
-    float4 part[kClMaxCta];
+    constexpr int kHalf = kClMaxCta / 2;
+    float4 part[kHalf];
 #pragma unroll
-    for (int q = 0; q < kClMaxCta; ++q)
-      part[q] = (q < (int)CP) ? ld_cluster_f4(cl_map(&sh.W[i][4 * cq], (uint32_t)q)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < kHalf; ++q) {
+      const int src = half * kHalf + q;
+      part[q] = (src < (int)CP) ? ld_cluster_f4(cl_map(&sh.W[i][4 * cq], (uint32_t)src)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float4 tot = part[0];
 #pragma unroll
-    for (int q = 1; q < kClMaxCta; ++q) {
+    for (int q = 1; q < kHalf; ++q) {
       tot.x += part[q].x;
       tot.y += part[q].y;
       tot.z += part[q].z;
       tot.w += part[q].w;
     }
-    sh.Wt[i][4 * cq] = tot.x;
-    sh.Wt[i][4 * cq + 1] = tot.y;
-    sh.Wt[i][4 * cq + 2] = tot.z;
-    sh.Wt[i][4 * cq + 3] = tot.w;
+    if (half == 1) *reinterpret_cast<float4*>(&sh.Wh[i][4 * cq]) = tot;
+    __syncthreads();
+    if (half == 0) {
+      const float4 hi = *reinterpret_cast<const float4*>(&sh.Wh[i][4 * cq]);
+      sh.Wt[i][4 * cq] = tot.x + hi.x;
+      sh.Wt[i][4 * cq + 1] = tot.y + hi.y;
+      sh.Wt[i][4 * cq + 2] = tot.z + hi.z;
+      sh.Wt[i][4 * cq + 3] = tot.w + hi.w;
+    }
   }
   __syncthreads();
-  {
+  if (half == 0) {
     float y[4] = {0.f, 0.f, 0.f, 0.f};
     for (int c = 0; c <= i; ++c) {
       const float t = sh.T[c][i];
@@ -154,12 +167,13 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
     *reinterpret_cast<float4*>(&sh.W2[i][4 * cq]) = make_float4(y[0], y[1], y[2], y[3]);
   }
   __syncthreads();
-  // (4) C_p - V_p W2, one row per thread, back through shared memory.
+  // (4) C_p - V_p W2: row tid % 256, columns 16 (tid / 256) .. + 15, back through shared memory.
   {
-    float out[32];
+    const int row = tid & (kU1Rows - 1), cb = 16 * half;
+    float out[16];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 x = *reinterpret_cast<const float4*>(&sh.C[tid][4 * q]);
+    for (int q = 0; q < 4; ++q) {
+      const float4 x = *reinterpret_cast<const float4*>(&sh.C[row][cb + 4 * q]);
       out[4 * q] = x.x;
       out[4 * q + 1] = x.y;
       out[4 * q + 2] = x.z;
@@ -167,13 +181,13 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
     }
 #pragma unroll 2
     for (int c4 = 0; c4 < 32; c4 += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(&sh.V[tid][c4]);
+      const float4 v = *reinterpret_cast<const float4*>(&sh.V[row][c4]);
       const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 y = *reinterpret_cast<const float4*>(&sh.W2[c4 + a][4 * q]);
+        for (int q = 0; q < 4; ++q) {
+          const float4 y = *reinterpret_cast<const float4*>(&sh.W2[c4 + a][cb + 4 * q]);
           out[4 * q] = fmaf(-vv[a], y.x, out[4 * q]);
           out[4 * q + 1] = fmaf(-vv[a], y.y, out[4 * q + 1]);
           out[4 * q + 2] = fmaf(-vv[a], y.z, out[4 * q + 2]);
@@ -182,13 +196,13 @@ __global__ void __launch_bounds__(256) wy_u1_kernel(WyParams P) {
       }
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
-      *reinterpret_cast<float4*>(&sh.C[tid][4 * q]) = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<float4*>(&sh.C[row][cb + 4 * q]) = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
   }
   __syncthreads();
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int e = it * 256 + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
+  for (int it = 0; it < 4; ++it) {
+    const int e = it * kU1Threads + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
     if (r < m && c0 + c < nc)
       *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + c0 + c) =
           *reinterpret_cast<const float4*>(&sh.C[rr][c]);
