@@ -564,11 +564,12 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
 }
 
 // Look-ahead streams: the critical chain (panels, narrow updates, T, Y and the update of the
-// next outer block's columns) runs on a high-priority stream, the rest of each wide update on a
-// low-priority one, forked from and joined back into the caller's stream.
+// next outer block's or panel's columns) runs on a high-priority stream p, the rest of each
+// update on a low-priority one u, and (single-level schedule) the strip of the panel after next
+// on a second high-priority stream m; all forked from and joined back into the caller's stream.
 struct LookaheadStreams {
-  cudaStream_t p = nullptr, u = nullptr;
-  cudaEvent_t fork = nullptr, y = nullptr, u2 = nullptr, pj = nullptr, uj = nullptr;
+  cudaStream_t p = nullptr, u = nullptr, m = nullptr;  // critical, bulk update, strip update
+  cudaEvent_t fork = nullptr, y = nullptr, u2 = nullptr, u2a = nullptr, pj = nullptr, uj = nullptr, mj = nullptr;
 };
 constexpr int kMaxDevices = 64;
 
@@ -612,7 +613,8 @@ static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
     int least = 0, greatest = 0;
     cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
     if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&L.u, cudaStreamNonBlocking, least);
-    for (cudaEvent_t* ev : {&L.fork, &L.y, &L.u2, &L.pj, &L.uj})
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&L.m, cudaStreamNonBlocking, greatest);
+    for (cudaEvent_t* ev : {&L.fork, &L.y, &L.u2, &L.u2a, &L.pj, &L.uj, &L.mj})
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&L.p, cudaStreamNonBlocking, greatest);
     if (e != cudaSuccess) {
@@ -795,22 +797,29 @@ static cudaError_t run_two_level(const float* A, float* H, float* tau, long long
   return body != cudaSuccess ? body : e;
 }
 
-// Single-level blocked QR with look-ahead: after panel k (32 columns at kb), U1 updates the
-// next panel's 32 columns on the critical stream sp and U2 everything right of them on su, so
-// U2 of panel k runs while panel k + 1 is factored. U1 of panel k + 1 waits for U2 of panel k
-// (same columns). Panel T factors alternate between two slots of the workspace (U2 of panel k
-// may still read slot k % 2 while panel k + 1 writes the other one); U1 and U2 of one panel use
-// disjoint columns of the partial-product buffers. L == nullptr runs everything on sp.
+// Single-level blocked QR with look-ahead of depth two. After panel k (32 columns at kb) its
+// update is cut in three column ranges:
+//   U1(k)  = [kb + 32, kb + 64), the next panel's columns, on the critical stream sp;
+//   U2a(k) = [kb + 64, kb + 96), the panel after next, one clustered launch on stream sm;
+//   U2b(k) = [kb + 96, n), everything else, on the low-priority stream su.
+// Dependencies: U1(k) waits for U2a(k - 1) (same columns, previous panel); U2a(k) waits for
+// panel k and U2b(k - 1) (its columns carry panel k - 1's update from there); U2b(k) follows
+// U2b(k - 1) on su. So the bulk update U2b of panel k - 1 has until U1(k + 1) -- two panel steps
+// -- to finish, instead of one. Panel T factors rotate over three workspace slots (U2b(k - 1) may
+// still read slot k - 1 while panel k + 1 writes its own); the partial-product buffers of the
+// three-kernel update are indexed by column relative to the panel, and U1, U2a and U2b of one
+// panel as well as U2b(k - 1) use disjoint index ranges. L == nullptr runs the same three
+// launches on sp, so both schedules give bitwise the same result.
 static cudaError_t single_level_body(const float* A, float* H, float* tau, long long batch, int n, long long abs,
                                      const Workspace& ws, cudaStream_t sp, cudaStream_t su, LookaheadStreams* L) {
   cudaError_t e;
-  bool u2_pending = false;
+  bool pending = false;  // U2a / U2b of the previous panel have been enqueued on the side streams
   constexpr long long kTStride = 4 * kNB * kNB;
   for (int kb = 0; kb < n; kb += kNB) {
     const int w = std::min(kNB, n - kb), m = n - kb, nc = n - kb - w;
     const float* src = (kb == 0) ? A : H;
     const long long sbs = (kb == 0) ? abs : (long long)n * n;
-    float* Tslot = ws.T + (size_t)((kb / kNB) & 1) * kNB * kNB;
+    float* Tslot = ws.T + (size_t)((kb / kNB) % 3) * kNB * kNB;
     PanelParams pp{src, sbs, H, tau, nc > 0 ? Tslot : nullptr, n, kb, w};
     {
       LaunchScope ls(panel_kind(m), batch * panel_flops(m, w), batch * 8.0 * m * w);
@@ -818,25 +827,30 @@ static cudaError_t single_level_body(const float* A, float* H, float* tau, long 
     }
     if (e != cudaSuccess) return e;
     if (nc <= 0) continue;
-    if (L == nullptr || nc <= kNB) {
-      // Same two launches as under look-ahead (next panel's columns, then the rest), so both
-      // schedules give bitwise the same result.
-      if (L != nullptr && u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;
-      u2_pending = false;
-      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, std::min(n, kb + w + kNB), sp, true)) !=
-          cudaSuccess)
+    const int c1 = std::min(n, kb + w + kNB), c2 = std::min(n, kb + w + 2 * kNB);
+    if (L == nullptr) {
+      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, c1, sp, true)) != cudaSuccess) return e;
+      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, c2, sp, true)) != cudaSuccess) return e;
+      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 2 * kNB, n, sp, true)) != cudaSuccess)
         return e;
-      if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, n, sp, true)) != cudaSuccess) return e;
       continue;
     }
     if ((e = cudaEventRecord(L->y, sp)) != cudaSuccess) return e;
-    if (u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;  // U2 of panel k - 1
-    if ((e = cudaStreamWaitEvent(su, L->y, 0)) != cudaSuccess) return e;
-    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, n, su, true)) != cudaSuccess) return e;
-    if ((e = cudaEventRecord(L->u2, su)) != cudaSuccess) return e;
-    u2_pending = true;
-    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, kb + w + kNB, sp, true)) != cudaSuccess)
+    // U1(k) after U2a(k - 1) (the event still holds that record here).
+    if (pending && (e = cudaStreamWaitEvent(sp, L->u2a, 0)) != cudaSuccess) return e;
+    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 0, c1, sp, true)) != cudaSuccess) return e;
+    // U2a(k) after panel k and U2b(k - 1).
+    if ((e = cudaStreamWaitEvent(L->m, L->y, 0)) != cudaSuccess) return e;
+    if (pending && (e = cudaStreamWaitEvent(L->m, L->u2, 0)) != cudaSuccess) return e;
+    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, kNB, c2, L->m, true)) != cudaSuccess)
       return e;
+    if ((e = cudaEventRecord(L->u2a, L->m)) != cudaSuccess) return e;
+    // U2b(k) after panel k.
+    if ((e = cudaStreamWaitEvent(su, L->y, 0)) != cudaSuccess) return e;
+    if ((e = launch_wy(src, sbs, H, Tslot, kTStride, ws, batch, n, kb, w, 2 * kNB, n, su, true)) != cudaSuccess)
+      return e;
+    if ((e = cudaEventRecord(L->u2, su)) != cudaSuccess) return e;
+    pending = true;
   }
   return cudaSuccess;
 }
@@ -854,11 +868,14 @@ static cudaError_t with_lookahead(int dev, cudaStream_t s, Body body) {
   if ((e = cudaEventRecord(L->fork, s)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->p, L->fork, 0)) != cudaSuccess) return e;
   if ((e = cudaStreamWaitEvent(L->u, L->fork, 0)) != cudaSuccess) return e;
+  if ((e = cudaStreamWaitEvent(L->m, L->fork, 0)) != cudaSuccess) return e;
   const cudaError_t b = body(L);
   e = cudaEventRecord(L->pj, L->p);
   if (e == cudaSuccess) e = cudaEventRecord(L->uj, L->u);
+  if (e == cudaSuccess) e = cudaEventRecord(L->mj, L->m);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->pj, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->uj, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, L->mj, 0);
   return b != cudaSuccess ? b : e;
 }
 
