@@ -25,6 +25,16 @@
 
 namespace qrb200 {
 
+// Volatile shared float4 load: issued where it stands, so a long unrolled loop does not hoist
+// all of its loads ahead of the arithmetic (which would need a register per loaded value).
+__device__ __forceinline__ float4 lds4_inorder(const float* p) {
+  float4 v;
+  asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
 template <int RPL>
 struct __align__(16) PanelFwShared {
   static constexpr int R = 32 * RPL;

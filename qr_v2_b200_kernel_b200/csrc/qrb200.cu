@@ -448,7 +448,7 @@ static int num_sms() {
 // update inside an outer block, or either half of a single-level look-ahead update). T factors
 // sit t_bstride elements apart. Aligned rows: a short update (<= 128 columns, allow_u1) is one
 // clustered launch (wy_u1: V^T C partials per 256-row CTA summed over DSMEM, T^T, update);
-// otherwise V^T C (tcgen05 beyond 128 columns, else FP32), T^T sum, FP32 update with one tile
+// otherwise V^T C (tcgen05 beyond 64 columns, else FP32), T^T sum, FP32 update with one tile
 // per CTA for wide updates (a persistent grid that filled every SM before the next
 // high-priority panel launched held that panel back). Unaligned rows: wy_simt.cuh.
 static cudaError_t launch_wy(const float* src, long long sbs, float* H, const float* T, long long t_bstride,
@@ -516,7 +516,9 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     return launch_k(wy_u1_kernel, dim3((unsigned)cp, (unsigned)cdiv(ncl, 32), (unsigned)batch), dim3(kU1Threads), kU1Smem, s,
                     (unsigned)cp, true, wp);
   }
-  const bool vtc_tc = vec && ncl > kV2Cols;  // wide V^T C on tcgen05, partials stored transposed
+  // V^T C on tcgen05 (partials stored transposed) above 64 columns: the narrow updates of 96
+  // columns and the single-level tails as well (C2 4.32 -> 4.25 ms on B200).
+  const bool vtc_tc = vec && ncl > 64;
   {
     LaunchScope ls(K_VTC, 2.0 * bm * w * ncl, 4.0 * bm * (w + ncl) + 4.0 * batch * wp.nsplit * w * (double)ncl);
     if (vtc_tc)

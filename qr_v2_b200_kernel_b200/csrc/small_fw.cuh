@@ -2,23 +2,26 @@
 // registers -- the one-CTA-per-matrix path of the reference's fused kernel
 // (submission.py:72-175), restructured as a factor warp fed by update warps.
 //
-// The columns are cut into blocks of 4. Warp 0, the factor warp, runs the serial chain: for
-// block t it takes the block (every earlier block reflector but the last already applied),
-// applies the last one itself, factors the 4 columns with warp shuffles only (larfg/larf,
-// submission.py:91-107, and the LARFT recurrence for the 4 x 4 T, :129-137), writes the
-// finished block to H and publishes V_t and T_t in shared memory. Update warps own the later
-// blocks (block t0 = u + 1, then t0 + NU when the matrix has that many) and apply each
-// published block reflector to them (compact WY, C <- C - V T^T (V^T C),
-// milestones/01_eager_official123203us.py:102-107), handing block t to the factor warp once
-// V_0 .. V_{t-2} are in. Warps 4, 8, ... stay idle: warps share a scheduler when their indices
-// agree mod 4, so the factor warp gets one of the four schedulers to itself.
+// The columns are cut into blocks of 4. Warp 0, the factor warp, runs the serial chain: it takes
+// block t with every earlier reflector already applied, factors its 4 columns with warp shuffles
+// only (larfg/larf, submission.py:91-107, and the LARFT recurrence for the 4 x 4 T, :129-137) and
+// publishes each reflector v_j and tau_j in shared memory the moment it is formed, then the
+// block's T_t, and writes the finished block to H. Update warps own the later blocks (block
+// t0 = u + 1, then t0 + NU when the matrix has that many). The update warp holding block t + 1
+// applies V_0 .. V_{t-1} as block reflectors (compact WY, C <- C - V T^T (V^T C),
+// milestones/01_eager_official123203us.py:102-107) as they are published, then the reflectors of
+// block t one by one (x <- x - tau v (v^T x)) while the factor warp is still forming them, and
+// hands the block over: when the factor warp finishes block t, block t + 1 is ready but for the
+// last reflector's rank-one update, and the factor warp itself applies nothing. Warps 4, 8, ...
+// stay idle: warps share a scheduler when their indices agree mod 4, so the factor warp gets one
+// of the four schedulers to itself.
 //
 // Hand-offs are counters in shared memory written with release and polled with acquire
-// semantics: vcount (V blocks published; every V stays in shared memory, so a consumer can
-// fall behind without holding up the factor warp) and bflag[2] (the block in each slot of the
-// two-slot B ring; a slot is reused for block t + 2 only after V_t is out, i.e. after the factor
-// warp has read block t). Every wait is bounded; on expiry the warp records a device status
-// and leaves.
+// semantics: rcount (reflectors published), vcount (blocks whose V and T are complete; every V
+// stays in shared memory, so a consumer can fall behind without holding up the factor warp) and
+// bflag[2] (the block in each slot of the two-slot B ring; a slot is reused for block t + 2 only
+// after the factor warp has read block t, which precedes V_t). Every wait is bounded; on expiry
+// the warp records a device failure and leaves.
 #pragma once
 
 #include "common.cuh"
@@ -76,9 +79,13 @@ __device__ __forceinline__ void fw_publish(int* p, int v) {
 // Factor the block (global columns c0 ..); T (every lane holds all of it), tau written.
 // J32: every pivot row is < 32 (a panel of at most 32 columns), so rows 32 i, i >= 1, are
 // always below the pivot and register 0 holds the pivot row.
+// Vpub (may be null): [column][row] storage of the block's masked reflectors; each column's
+// v_j and tau_j go there (and to tpub[j]) and *rcount is released to j + 1 as soon as the
+// reflector is formed.
 template <int CPW, int RPL, bool J32 = false>
 __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int c0, const int n, float (&Tw)[CPW][CPW],
-                                                float* __restrict__ taub) {
+                                                float* __restrict__ taub, float* Vpub = nullptr,
+                                                float* tpub = nullptr, int* rcount = nullptr) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < CPW; ++k)
@@ -124,6 +131,16 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
 #pragma unroll
       for (int c = 0; c <= CPW; ++c) d[c] += __shfl_xor_sync(kFullMask, d[c], o);
     const Reflector rf = make_reflector_fast(rowj[jj], d[jj], d[CPW]);
+    if (Vpub != nullptr) {
+      constexpr int LD = 32 * RPL;
+#pragma unroll
+      for (int i = 0; i < RPL; ++i) {
+        const int r = lane + 32 * i;
+        Vpub[jj * LD + r] = (r > j) ? xm[i] * rf.scale : (r == j ? 1.f : 0.f);
+      }
+      if (lane == 0) tpub[j] = rf.tau;
+      fw_publish(rcount, j + 1);
+    }
     float z[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
@@ -155,71 +172,6 @@ __device__ __forceinline__ void fw_factor_block(float (&a)[CPW][RPL], const int 
   }
 }
 
-// Factor-warp layout: a <- (I - V T V^T)^T a, V (masked: unit diagonal, zeros above;
-// [column][row]) and T (row-major) in shared memory. The 16 partial products W[cp][c] are
-// summed across the warp with a transposed butterfly (each xor step halves the live values:
-// 16 shuffles instead of 80), then broadcast back from the lanes that hold them.
-template <int NMAX, int CPW, int RPL>
-__device__ __forceinline__ void fw_apply_cols(float (&a)[CPW][RPL], const float* __restrict__ Vs,
-                                              const float* __restrict__ Ts) {
-  static_assert(CPW == 4, "transposed reduction assumes 4 x 4 products");
-  const int lane = threadIdx.x & 31;
-  float vm[CPW][RPL];
-#pragma unroll
-  for (int cp = 0; cp < CPW; ++cp)
-#pragma unroll
-    for (int i = 0; i < RPL; ++i) vm[cp][i] = Vs[cp * NMAX + lane + 32 * i];
-  float p[16];  // p[4 cp + c] = this lane's share of V[:, cp] . a[:, c]
-#pragma unroll
-  for (int cp = 0; cp < CPW; ++cp)
-#pragma unroll
-    for (int c = 0; c < CPW; ++c) {
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < RPL; ++i) acc = fmaf(vm[cp][i], a[c][i], acc);
-      p[cp * CPW + c] = acc;
-    }
-  // Steps o = 16, 8, 4, 2 keep the half of the values selected by the lane's bit; after them
-  // lane l holds value ((l >> 1) & 15) summed over 16 lanes, and o = 1 completes the sum.
-#pragma unroll
-  for (int step = 0; step < 4; ++step) {
-    const int o = 16 >> step, half = 8 >> step;
-    const bool up = (lane & o) != 0;
-#pragma unroll
-    for (int q = 0; q < half; ++q) {
-      const float send = up ? p[q] : p[q + half];
-      const float keep = up ? p[q + half] : p[q];
-      p[q] = keep + __shfl_xor_sync(kFullMask, send, o);
-    }
-  }
-  p[0] += __shfl_xor_sync(kFullMask, p[0], 1);
-  // Value v sits in the lanes whose bits 4..1 spell v: bit 4 chose the upper half first, so
-  // v = 8 b4 + 4 b3 + 2 b2 + b1.
-  float W[CPW][CPW];
-#pragma unroll
-  for (int v = 0; v < 16; ++v) W[v / CPW][v % CPW] = __shfl_sync(kFullMask, p[0], 2 * v);
-#pragma unroll
-  for (int c = 0; c < CPW; ++c)
-#pragma unroll
-    for (int cp = 0; cp < CPW; ++cp) {
-      float y = 0.f;
-#pragma unroll
-      for (int k = 0; k <= cp; ++k) y = fmaf(Ts[k * CPW + cp], W[k][c], y);
-#pragma unroll
-      for (int i = 0; i < RPL; ++i) a[c][i] = fmaf(-vm[cp][i], y, a[c][i]);
-    }
-}
-
-// Volatile shared float4 load: issued where it stands, so a long unrolled loop does not hoist
-// all of its loads ahead of the arithmetic (which would need a register per loaded value).
-__device__ __forceinline__ float4 lds4_inorder(const float* p) {
-  float4 v;
-  asm volatile("ld.volatile.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
-
 // Update-warp layout: lane 4 g + c holds column c, rows 32 q + 4 g + e (q < RPG / 4, e < 4) in
 // x[4 q + e]. The dot products V^T x reduce over the 8 lanes of a column (3 shuffle levels), and
 // the 8 row groups of one float4 load are 8 consecutive 16-byte pieces (no bank conflicts).
@@ -233,7 +185,7 @@ __device__ __forceinline__ void fw_apply_rows(float (&x)[RPG], const float* __re
   for (int k = 0; k < RPG; k += 4) {
 #pragma unroll
     for (int cp = 0; cp < CPW; ++cp) {
-      const float4 v = lds4_inorder(Vs + cp * NMAX + 8 * k + g4);
+      const float4 v = *reinterpret_cast<const float4*>(Vs + cp * NMAX + 8 * k + g4);
       W[cp] = fmaf(v.x, x[k], W[cp]);
       W[cp] = fmaf(v.y, x[k + 1], W[cp]);
       W[cp] = fmaf(v.z, x[k + 2], W[cp]);
@@ -256,7 +208,7 @@ __device__ __forceinline__ void fw_apply_rows(float (&x)[RPG], const float* __re
   for (int k = 0; k < RPG; k += 4) {
 #pragma unroll
     for (int cp = 0; cp < CPW; ++cp) {
-      const float4 v = lds4_inorder(Vs + cp * NMAX + 8 * k + g4);
+      const float4 v = *reinterpret_cast<const float4*>(Vs + cp * NMAX + 8 * k + g4);
       x[k] = fmaf(-v.x, Y[cp], x[k]);
       x[k + 1] = fmaf(-v.y, Y[cp], x[k + 1]);
       x[k + 2] = fmaf(-v.z, Y[cp], x[k + 2]);
@@ -265,12 +217,40 @@ __device__ __forceinline__ void fw_apply_rows(float (&x)[RPG], const float* __re
   }
 }
 
+// Update-warp layout: x <- (I - tau v v^T) x for one published reflector (v in shared memory,
+// masked); the dot v^T x reduces over the 8 lanes of a column (3 shuffle levels).
+template <int NMAX, int RPG>
+__device__ __forceinline__ void fw_apply_reflector_rows(float (&x)[RPG], const float* __restrict__ v, float tau,
+                                                        int g4) {
+  float wv = 0.f;
+#pragma unroll
+  for (int k = 0; k < RPG; k += 4) {
+    const float4 vv = *reinterpret_cast<const float4*>(v + 8 * k + g4);
+    wv = fmaf(vv.x, x[k], wv);
+    wv = fmaf(vv.y, x[k + 1], wv);
+    wv = fmaf(vv.z, x[k + 2], wv);
+    wv = fmaf(vv.w, x[k + 3], wv);
+  }
+#pragma unroll
+  for (int o = 4; o <= 16; o <<= 1) wv += __shfl_xor_sync(kFullMask, wv, o);
+  const float f = tau * wv;
+#pragma unroll
+  for (int k = 0; k < RPG; k += 4) {
+    const float4 vv = *reinterpret_cast<const float4*>(v + 8 * k + g4);
+    x[k] = fmaf(-vv.x, f, x[k]);
+    x[k + 1] = fmaf(-vv.y, f, x[k + 1]);
+    x[k + 2] = fmaf(-vv.z, f, x[k + 2]);
+    x[k + 3] = fmaf(-vv.w, f, x[k + 3]);
+  }
+}
+
 template <int NMAX, int CPW>
 struct __align__(16) SmallFwShared {
   float V[NMAX / CPW][CPW][NMAX];  // every block's masked V ([column][row])
   float T[NMAX / CPW][CPW][CPW];
   float B[2][CPW][NMAX];           // blocks on their way to the factor warp
-  int vcount, bflag[2];
+  float tauv[NMAX];                // tau of every published reflector
+  int rcount, vcount, bflag[2];
 };
 
 template <int NMAX>
@@ -296,6 +276,7 @@ __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restr
   const bool vec = (n & 3) == 0 && (a_bstride & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(H)) & 15u) == 0;
   if (threadIdx.x == 0) {
+    sh.rcount = 0;
     sh.vcount = 0;
     sh.bflag[0] = sh.bflag[1] = -1;
   }
@@ -339,7 +320,7 @@ __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restr
     };
     for (int t = 0; t < nb; ++t) {
       const int c0 = t * CPW;
-      if (t >= 1) {
+      if (t >= 1) {  // block t arrives with every earlier reflector applied
         const int sl = t & 1;
         if (!fw_wait_geq(&sh.bflag[sl], t)) return;
 #pragma unroll
@@ -347,18 +328,39 @@ __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restr
 #pragma unroll
           for (int i = 0; i < RPL; ++i) a[c][i] = sh.B[sl][c][lane + 32 * i];
         store_block(t - 1);
-        fw_apply_cols<NMAX, CPW, RPL>(a, &sh.V[t - 1][0][0], &sh.T[t - 1][0][0]);  // V_{t-1}
+        // The last reflector of block t - 1 (v below its diagonal in hprev[CPW - 1], tau in
+        // tauv): a <- a - tau v (v^T a), one butterfly for the four dots.
+        const int jl = c0 - 1;
+        const float tl = sh.tauv[jl];
+        float vl[RPL];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+          const int r = lane + 32 * i;
+          vl[i] = (r > jl) ? hprev[CPW - 1][i] : (r == jl ? 1.f : 0.f);
+        }
+        float dl[CPW];
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < RPL; ++i) acc = fmaf(vl[i], a[c][i], acc);
+          dl[c] = acc;
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+          for (int c = 0; c < CPW; ++c) dl[c] += __shfl_xor_sync(kFullMask, dl[c], o);
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          const float f = tl * dl[c];
+#pragma unroll
+          for (int i = 0; i < RPL; ++i) a[c][i] = fmaf(-f, vl[i], a[c][i]);
+        }
       }
       float Tw[CPW][CPW];
-      fw_factor_block<CPW, RPL>(a, c0, n, Tw, taub);
-      if (t + 1 < nb) {  // publish V_t (masked) and T_t
-#pragma unroll
-        for (int c = 0; c < CPW; ++c)
-#pragma unroll
-          for (int i = 0; i < RPL; ++i) {
-            const int r = lane + 32 * i;
-            sh.V[t][c][r] = (r > c0 + c) ? a[c][i] : (r == c0 + c ? 1.f : 0.f);
-          }
+      const bool more = t + 1 < nb;  // a later block needs this one's reflectors
+      fw_factor_block<CPW, RPL>(a, c0, n, Tw, taub, more ? &sh.V[t][0][0] : nullptr, sh.tauv, &sh.rcount);
+      if (more) {  // publish T_t (V_t went out column by column)
         if (lane == 0)
 #pragma unroll
           for (int k = 0; k < CPW; ++k)
@@ -391,8 +393,17 @@ __global__ void __launch_bounds__(32 * NWL) small_fw_kernel(const float* __restr
       if (!(P_SLEEP_NS > 0 ? fw_wait_geq_pause(&sh.vcount, s + 1, P_SLEEP_NS) : fw_wait_geq(&sh.vcount, s + 1))) return;
       fw_apply_rows<NMAX, CPW, RPG>(x, &sh.V[s][0][0], &sh.T[s][0][0], g4);
     }
-    // Slot t & 1 last held block t - 2, which the factor warp read before publishing V_{t-2}:
-    // the wait for V_{t-2} above already covers its reuse.
+    // Block t - 1 is being factored: apply its reflectors one by one as they come out, all but
+    // the last, which the factor warp applies itself once it has the block.
+#pragma unroll 1
+    for (int jj = 0; jj < CPW - 1; ++jj) {
+      const int j = (t - 1) * CPW + jj;
+      if (j >= n) break;
+      if (!fw_wait_geq(&sh.rcount, j + 1)) return;
+      fw_apply_reflector_rows<NMAX, RPG>(x, &sh.V[t - 1][jj][0], sh.tauv[j], g4);
+    }
+    // Slot t & 1 last held block t - 2, which the factor warp read before it published the
+    // first reflector of block t - 1: the waits above already cover its reuse.
     const int sl = t & 1;
 #pragma unroll
     for (int k = 0; k < RPG; k += 4)
