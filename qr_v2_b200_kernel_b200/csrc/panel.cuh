@@ -143,72 +143,73 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
                                                    OwnerShared<RPL, CPW>& sh, float* __restrict__ tau_out) {
   constexpr int NW = 32 / CPW;
   const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
-  for (int j = 0; j < jmax; ++j) {
-    const int ph = j & 1;
-    if (g == j % NW) {
-      const int oq = j / NW;
-      float x[RPL];
+  // Reflector j = NW oq + jg is owned by warp jg as its register column oq. The loop over oq is
+  // unrolled, so the owner's column and, for every warp, whether each of its columns lies left
+  // of, at or right of j are compile-time facts except within the group oq itself.
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) {
-        float t = a[0][i];
+  for (int oq = 0; oq < CPW; ++oq) {
+#pragma unroll 1
+    for (int jg = 0; jg < NW; ++jg) {
+      const int j = NW * oq + jg;
+      if (j >= jmax) break;
+      const int ph = j & 1;
+      if (g == jg) {
+        // Four independent partial sums shorten the dependent FMA chain.
+        float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int q = 1; q < CPW; ++q) t = (q == oq) ? a[q][i] : t;
-        x[i] = t;
+        for (int i = 0; i < RPL; ++i)
+          sp[i & 3] = (lane + 32 * i > j) ? fmaf(a[oq][i], a[oq][i], sp[i & 3]) : sp[i & 3];
+        float s = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
+        const float alpha = __shfl_sync(kFullMask, a[oq][0], j);
+        const Reflector rf = make_reflector_fast(alpha, s);
+        if (lane == 0 && fmaf(alpha, alpha, s) < kRescaleDown) sh.tiny = 1;  // see panel_owner_kernel
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+          const int lr = lane + 32 * i;
+          const float vi = (lr > j) ? a[oq][i] * rf.scale : (lr == j ? 1.f : 0.f);
+          sh.v[ph][lr] = vi;
+          a[oq][i] = (lr > j) ? vi : (lr == j ? rf.diag : a[oq][i]);
+        }
+        if (lane == 0) {
+          sh.tau[j] = rf.tau;
+          tau_out[j] = rf.tau;
+        }
       }
-      // Four independent partial sums shorten the dependent FMA chain.
-      float sp[4] = {0.f, 0.f, 0.f, 0.f};
+      __syncthreads();
+      const float tj = sh.tau[j];
+      float v[RPL];
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) sp[i & 3] = (lane + 32 * i > j) ? fmaf(x[i], x[i], sp[i & 3]) : sp[i & 3];
-      float s = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+      for (int i = 0; i < RPL; ++i) v[i] = sh.v[ph][lane + 32 * i];
+      float dq[CPW];
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(kFullMask, s, o);
-      const float alpha = __shfl_sync(kFullMask, x[0], j);
-      const Reflector rf = make_reflector_fast(alpha, s);
-      if (lane == 0 && fmaf(alpha, alpha, s) < kRescaleDown) sh.tiny = 1;  // see panel_owner_kernel
+      for (int q = 0; q < CPW; ++q) {
+        float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) {
-        const int lr = lane + 32 * i;
-        const float vi = (lr > j) ? x[i] * rf.scale : (lr == j ? 1.f : 0.f);
-        sh.v[ph][lr] = vi;
-        const float nx = (lr > j) ? vi : (lr == j ? rf.diag : x[i]);
-#pragma unroll
-        for (int q = 0; q < CPW; ++q)
-          if (q == oq) a[q][i] = nx;
+        for (int i = 0; i < RPL; i += 2) {
+          d0 = fmaf(v[i], a[q][i], d0);
+          if (i + 1 < RPL) d1 = fmaf(v[i + 1], a[q][i + 1], d1);
+        }
+        dq[q] = d0 + d1;
       }
-      if (lane == 0) {
-        sh.tau[j] = rf.tau;
-        tau_out[j] = rf.tau;
-      }
-    }
-    __syncthreads();
-    const float tj = sh.tau[j];
-    float v[RPL];
 #pragma unroll
-    for (int i = 0; i < RPL; ++i) v[i] = sh.v[ph][lane + 32 * i];
-    float dq[CPW];
+      for (int o = 16; o >= 1; o >>= 1)
 #pragma unroll
-    for (int q = 0; q < CPW; ++q) {
-      float d0 = 0.f, d1 = 0.f;
+        for (int q = 0; q < CPW; ++q) dq[q] += __shfl_xor_sync(kFullMask, dq[q], o);
 #pragma unroll
-      for (int i = 0; i < RPL; i += 2) {
-        d0 = fmaf(v[i], a[q][i], d0);
-        if (i + 1 < RPL) d1 = fmaf(v[i + 1], a[q][i + 1], d1);
-      }
-      dq[q] = d0 + d1;
-    }
+      for (int q = 0; q < CPW; ++q) {
+        const int c = g + NW * q;
+        // q > oq: c > j; q < oq: c < j; q == oq: decided by g against jg.
+        const bool right = (q > oq) || (q == oq && g > jg);
+        const bool left = (q < oq) || (q == oq && g < jg);
+        if (right && c < w) {
+          const float f = tj * dq[q];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-      for (int q = 0; q < CPW; ++q) dq[q] += __shfl_xor_sync(kFullMask, dq[q], o);
-#pragma unroll
-    for (int q = 0; q < CPW; ++q) {
-      const int c = g + NW * q;
-      if (c > j && c < w) {
-        const float f = tj * dq[q];
-#pragma unroll
-        for (int i = 0; i < RPL; ++i) a[q][i] = fmaf(-f, v[i], a[q][i]);
-      } else if (HAS_T && c < j) {
-        if (lane == 0) sh.G[c][j] = dq[q];
+          for (int i = 0; i < RPL; ++i) a[q][i] = fmaf(-f, v[i], a[q][i]);
+        } else if (HAS_T && left) {
+          if (lane == 0) sh.G[c][j] = dq[q];
+        }
       }
     }
   }

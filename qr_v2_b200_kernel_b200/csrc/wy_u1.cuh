@@ -63,19 +63,27 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
   const float* __restrict__ Sb = P.src + (long long)bidx * P.src_bstride;
   float* __restrict__ Ho = P.H + (long long)bidx * n * n;
 
-  // (1) stage V, C and T (8 threads per row, 16 bytes each); T's two loads per thread are
-  // issued first, so every load of the stage is in flight together.
+  // (1) stage V, C and T (8 threads per row, 16 bytes each): every global load of the stage is
+  // issued before the first shared-memory store, so the whole stage is in flight together.
   float tv[2];
 #pragma unroll
   for (int it = 0; it < 2; ++it) tv[it] = P.T[(long long)bidx * P.t_bstride + it * kU1Threads + tid];
+  float4 vs[4], xs[4];
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int e = it * kU1Threads + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), x = v;
+    vs[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+    xs[it] = vs[it];
     if (r < m) {
-      if (c < w) v = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
-      if (c0 + c < nc) x = *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + c0 + c);
+      if (c < w) vs[it] = *reinterpret_cast<const float4*>(Hb + (long long)(k + r) * n + k + c);
+      if (c0 + c < nc) xs[it] = *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * n + k + w + c0 + c);
     }
+  }
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int e = it * kU1Threads + tid, rr = e >> 3, q = e & 7, r = r0 + rr, c = 4 * q;
+    float4 v = vs[it];
+    const float4 x = xs[it];
     if (r < 32) {  // unit lower triangle at the top of the panel
       v.x = (c >= w) ? 0.f : (r > c ? v.x : (r == c ? 1.f : 0.f));
       v.y = (c + 1 >= w) ? 0.f : (r > c + 1 ? v.y : (r == c + 1 ? 1.f : 0.f));
@@ -207,8 +215,9 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
       *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + c0 + c) =
           *reinterpret_cast<const float4*>(&sh.C[rr][c]);
   }
-  // No CTA leaves while a peer may still read its partial.
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  // No CTA leaves while a peer may still read its partial. Relaxed: the peers' reads completed
+  // (their values were consumed) before they arrive, and nothing written here is read by a peer.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 }  // namespace qrb200
