@@ -252,10 +252,9 @@ static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch: a factor warp
-// fed by update warps (small_fw_kernel). Idle update warps pause kFwPollNs between polls, which
-// leaves issue slots to the factor warp, whose reflector chain is the kernel's critical path
-// (about 3 % faster on C1 than busy polling).
+// Whole-matrix factorisation by one CTA per matrix (n <= kSmallN), one launch: two factor
+// warps taking 4-column blocks in turn, fed by update warps (small_pp_kernel). Update warps
+// pause kFwPollNs between polls, which leaves issue slots to the factor warps.
 constexpr int kFwPollNs = 50;
 
 template <int NMAX, int NWL>
@@ -264,12 +263,12 @@ static cudaError_t launch_small_fw(const float* A, float* H, float* tau, long lo
   static PerDevice configured;
   const int dev = current_device();
   if (!configured.done(dev)) {
-    cudaError_t e = cudaFuncSetAttribute(small_fw_kernel<NMAX, NWL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)small_fw_smem<NMAX>());
+    cudaError_t e = cudaFuncSetAttribute(small_pp_kernel<NMAX, NWL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)small_pp_smem<NMAX>());
     if (e != cudaSuccess) return e;
     configured.mark(dev);
   }
-  small_fw_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_fw_smem<NMAX>(), s>>>(A, abs, H, tau, n, kFwPollNs);
+  small_pp_kernel<NMAX, NWL><<<(unsigned)batch, 32 * NWL, small_pp_smem<NMAX>(), s>>>(A, abs, H, tau, n, kFwPollNs);
   return cudaGetLastError();
 }
 
