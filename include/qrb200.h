@@ -140,13 +140,15 @@ int qrb200_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch
 
 /* ---- diagnostics (no counterpart in the reference; used by bench.py) ---------------- */
 
-/* The two 3xTF32 tcgen05 GEMMs of the 128-wide trailing update on their own, for accuracy
+/* The three 3xTF32 tcgen05 GEMMs of the 128-wide trailing update on their own, for accuracy
  * tests: for each matrix of H (batch x n x n, contiguous, 129 <= n <= 1024, n % 4 == 0),
  * V = the unit lower trapezoid of H[:, 0:128] (entries above the diagonal of that block read as
- * zero, the diagonal as one), C = H[:, 128:n]; computes C <- C - Y (V^T C) with Y given
- * (batch x n x 128, row-major), through W^T = C^T V (tc_vtc128) and C -= Y W (tc_upd128). The
- * first 128 columns of H are left as they are. Workspace as for qrb200_geqrf_f32(batch, n). */
-int qrb200_diag_wide_update_f32(float* H, const float* Y, int64_t batch, int64_t n, void* workspace,
+ * zero, the diagonal as one), C = H[:, 128:n]; computes C <- C - V (Tt (V^T C)) with the
+ * 128 x 128 matrix Tt given (batch x 128 x 128, row-major; the two-level schedule passes the
+ * block factor T transposed), through W^T = C^T V (tc_vtc128), W'^T = W^T Tt^T (tc_tw128) and
+ * C -= V W' (tc_upd128). The first 128 columns of H are left as they are. Workspace as for
+ * qrb200_geqrf_f32(batch, n). */
+int qrb200_diag_wide_update_f32(float* H, const float* Tt, int64_t batch, int64_t n, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
 /* Number of kernels this library has launched in the process so far (all threads). */

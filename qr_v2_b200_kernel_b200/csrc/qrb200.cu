@@ -49,14 +49,15 @@ constexpr int kMaxDevicesSm = 64;
 // records its algorithmic flops and bytes.
 enum KernelKind {
   K_PANEL = 0, K_SMALL, K_VTC, K_TW, K_UPD,
-  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_U1, K_PANEL_CL, K_LARFT, K_FILL, K_NUM_KINDS
+  K_GRAM, K_TBUILD, K_YGEMM, K_VTC128, K_UPD128, K_U1, K_PANEL_CL, K_LARFT, K_FILL, K_TW128, K_NUM_KINDS
 };
 static const char* const kKindName[K_NUM_KINDS] = {"panel_factor", "small_whole_matrix", "wy_vtc", "wy_tw", "wy_upd",
                                                    "tc_gram", "tbuild", "tc_ygemm", "tc_vtc128", "tc_upd128",
-                                                   "wy_u1", "panel_cluster", "larft_blocks", "fill_identity"};
+                                                   "wy_u1", "panel_cluster", "larft_blocks", "fill_identity",
+                                                   "tc_tw128"};
 // 1 = tensor-core contraction (FLOP bound); 0 = FP32 SIMT, memory or latency bound. (wy_vtc
 // counts the 32-wide V^T C, which runs on tcgen05 for wide updates but is HBM bound at K = 32.)
-static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 0, 0, 0, 1, 0, 1, 1, 1, 0, 0, 0, 0};
+static const int kKindTensorBound[K_NUM_KINDS] = {0, 0, 0, 0, 0, 1, 0, 1, 1, 1, 0, 0, 0, 0, 1};
 
 static std::atomic<long long> g_launches{0};
 
@@ -120,10 +121,13 @@ struct Workspace {
   float* T;     // single-level: batch x 32 x 32; two-level: panel factors batch x 4 x 32 x 32
   float* Wp;    // single-level / narrow-update partials: batch x nsplit x 32 x ncmax
   float* W2;    // batch x 32 x ncmax
-  float* Tob;   // two-level: batch x 128 x 128 outer-block factors
+  float* Tob;   // two-level: batch x 128 x 128 outer-block factors, stored transposed (even blocks)
+  float* Tob2;  // the same, odd outer blocks (the far update of a block still reads its factor
+                // while the next block's factor is assembled)
   float* Gp;    // two-level: batch x nsplit_g x 128 x 128 Gram partials
-  float* Y;     // two-level: batch x n x 128  (V T^T), even outer blocks
-  float* Y2;    // two-level: same, odd outer blocks (look-ahead keeps two blocks' Y alive)
+  float* Y;     // two-level: batch x n x 128, W'^T = (T^T V^T C)^T of the even outer blocks
+                // (row = trailing column); Y = V T^T for the accuracy diagnostic
+  float* Y2;    // two-level: same, odd outer blocks (look-ahead keeps two blocks' buffers alive)
   float* Wf;    // two-level: batch x nsplit_f x n x 128 (W^T partials of the wide update)
   size_t bytes;
 };
@@ -155,6 +159,7 @@ static Workspace layout(long long batch, int n, void* base) {
   // Wide-update buffers (sized for the largest n; unused on the single-level path).
   const int nsw = cdiv(n, kRowsPerSplitWide);
   ws.Tob = carve((size_t)batch * kOB * kOB * f);
+  ws.Tob2 = carve((size_t)batch * kOB * kOB * f);
   ws.Gp = carve((size_t)batch * nsw * kOB * kOB * f);
   ws.Y = carve((size_t)batch * n * kOB * f);
   ws.Y2 = carve((size_t)batch * n * kOB * f);
@@ -422,6 +427,8 @@ static cudaError_t tc128_configure() {
   if ((e = cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTbuildSmem)) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_WT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPDV, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   done.mark(dev);
   return cudaSuccess;
 }
@@ -628,14 +635,20 @@ static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
 }
 
 // 128-wide update of trailing columns [coff, cend - k0 - ow) (relative to k0 + ow) by the
-// outer block at k0: W^T = C^T V per row split, then C -= Y W. coff is a multiple of 128, so
-// every column sees the same tiles, and the same arithmetic, however the range is cut.
-static cudaError_t launch_wide(const float* src, long long sbs, float* H, const float* Y, const Workspace& ws,
-                               long long batch, int n, int k0, int ow, int coff, int cend, cudaStream_t s) {
+// outer block at k0, whose T factor is given transposed (Tt, batch x 128 x 128):
+//   W^T = C^T V per row split (tc_vtc128), W'^T = W^T T, i.e. W' = T^T V^T C (tc_tw128, into Wt,
+//   batch x n x 128, row = trailing column), then C -= V W' (tc_upd128).
+// Applying T to the (128 x columns) W' of each launch instead of forming Y = V T^T (rows x 128)
+// once per block keeps that product off the critical stream: the near update (the next block's
+// 128 columns) multiplies only its own columns. coff is a multiple of 128, so every column sees
+// the same tiles, and the same arithmetic, however the range is cut.
+static cudaError_t launch_wide(const float* src, long long sbs, float* H, const float* Tt, float* Wt,
+                               const Workspace& ws, long long batch, int n, int k0, int ow, int coff, int cend,
+                               cudaStream_t s) {
   const int m = n - k0, nc = cend - k0 - ow - coff;
   if (nc <= 0) return cudaSuccess;
   const int nsw = cdiv(m, kRowsPerSplitWide);
-  if (nsw > 2) return cudaErrorInvalidValue;  // the update tile sums at most two W^T partials
+  if (nsw > 2) return cudaErrorInvalidValue;  // the W^T T tile sums at most two W^T partials
   const double bm = (double)batch * m;
   WyParams wp{};
   wp.src = src;
@@ -655,8 +668,8 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   gp.src = src;
   gp.src_bstride = sbs;
   gp.Hout = H;
-  gp.T = ws.Tob;
-  gp.Y = const_cast<float*>(Y);
+  gp.T = Tt;
+  gp.Y = Wt;
   gp.y_bstride = (long long)n * kOB;
   gp.Wp = ws.Wf;
   gp.nsplit = nsw;
@@ -672,9 +685,15 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
     tc_vtcw_pipe_kernel<kOB, false, 3><<<grid, 128, vtcw_pipe_smem<kOB, false, 3>(), s>>>(wp);
   }
   {
-    LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * nsw * ow * (double)nc);
+    LaunchScope ls(K_TW128, 2.0 * batch * (double)nc * ow * ow,
+                   4.0 * batch * ((nsw + 1.0) * nc * ow + (double)ow * ow));
+    const dim3 grid(1, cdiv(nc, 128), (unsigned)batch);
+    tc_gemm128_pipe_kernel<MODE_WT, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
+  }
+  {
+    LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * ow * (double)nc);
     const dim3 grid(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch);
-    tc_gemm128_pipe_kernel<MODE_UPD, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
+    tc_gemm128_pipe_kernel<MODE_UPDV, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
   }
   return cudaGetLastError();
 }
@@ -715,7 +734,10 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
     const long long sbs = (k0 == 0) ? abs : (long long)n * n;
     const int nsw = cdiv(m, kRowsPerSplitWide);
     const double bm = (double)batch * m;
-    float* Y = ((k0 / kOB) & 1) ? ws.Y2 : ws.Y;
+    // Buffers alternate by block parity: the far update of this block may still read them while
+    // the next block's are written.
+    float* Wt = ((k0 / kOB) & 1) ? ws.Y2 : ws.Y;
+    float* Tt = ((k0 / kOB) & 1) ? ws.Tob2 : ws.Tob;
     // Gram matrix of the outer block's reflectors.
     WyParams g{};
     g.src = H;
@@ -735,39 +757,26 @@ static cudaError_t two_level_body(const float* A, float* H, float* tau, long lon
       tc_vtcw_pipe_kernel<kOB, true, 3><<<grid, 128, vtcw_pipe_smem<kOB, true, 3>(), sp>>>(g);
     }
     {
-      TbuildParams tp{ws.Gp, nsw, ws.T, ws.Tob, ow};
+      TbuildParams tp{ws.Gp, nsw, ws.T, Tt, ow, 1};  // T stored transposed
       LaunchScope ls(K_TBUILD, batch * 2.0 * ow * ow * ow / 3.0, 4.0 * batch * (nsw + 1.0) * ow * ow);
       tbuild_kernel<<<(unsigned)batch, 256, kTbuildSmem, sp>>>(tp);
-    }
-    Gemm128Params gp{};
-    gp.H = H;
-    gp.T = ws.Tob;
-    gp.Y = Y;
-    gp.y_bstride = (long long)n * kOB;
-    gp.n = n;
-    gp.k = k0;
-    gp.w = ow;
-    {
-      LaunchScope ls(K_YGEMM, 2.0 * bm * ow * ow, 4.0 * bm * ow * 2.0);
-      const dim3 grid(1, cdiv(m, 128), (unsigned)batch);
-      tc_gemm128_pipe_kernel<MODE_Y, 3><<<grid, 128, pipe128_smem<3>(), sp>>>(gp);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const int split_at = k0 + 2 * kOB;  // U1 = columns [k0 + ow, split_at), U2 = [split_at, n)
     if (L == nullptr || split_at >= n) {
       if (L != nullptr && u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;
       u2_pending = false;
-      e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, 0, n, sp);
+      e = launch_wide(src, sbs, H, Tt, Wt, ws, batch, n, k0, ow, 0, n, sp);
       if (e != cudaSuccess) return e;
       continue;
     }
     if ((e = cudaEventRecord(L->y, sp)) != cudaSuccess) return e;
     if (u2_pending && (e = cudaStreamWaitEvent(sp, L->u2, 0)) != cudaSuccess) return e;  // U2 of k0 - 128
     if ((e = cudaStreamWaitEvent(su, L->y, 0)) != cudaSuccess) return e;
-    if ((e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, kOB, n, su)) != cudaSuccess) return e;
+    if ((e = launch_wide(src, sbs, H, Tt, Wt, ws, batch, n, k0, ow, kOB, n, su)) != cudaSuccess) return e;
     if ((e = cudaEventRecord(L->u2, su)) != cudaSuccess) return e;
     u2_pending = true;
-    if ((e = launch_wide(src, sbs, H, Y, ws, batch, n, k0, ow, 0, split_at, sp)) != cudaSuccess) return e;
+    if ((e = launch_wide(src, sbs, H, Tt, Wt, ws, batch, n, k0, ow, 0, split_at, sp)) != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
@@ -1117,17 +1126,17 @@ int qrb200_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, 
 
 long long qrb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-int qrb200_diag_wide_update_f32(float* H, const float* Y, int64_t batch, int64_t n, void* workspace,
+int qrb200_diag_wide_update_f32(float* H, const float* Tt, int64_t batch, int64_t n, void* workspace,
                                 size_t workspace_bytes, void* stream) {
-  if (batch <= 0 || n <= kOB || n > 1024 || (n % 4) != 0 || batch > 65535 || !H || !Y) return QRB200_ERR_ARG;
-  if (((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(Y)) & 15u) != 0) return QRB200_ERR_ARG;
+  if (batch <= 0 || n <= kOB || n > 1024 || (n % 4) != 0 || batch > 65535 || !H || !Tt) return QRB200_ERR_ARG;
+  if (((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(Tt)) & 15u) != 0) return QRB200_ERR_ARG;
   const int dev_ok = check_device();
   if (dev_ok != QRB200_OK) return dev_ok;
   const Workspace ws = layout(batch, (int)n, workspace);
   if (!workspace || workspace_bytes < ws.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return QRB200_ERR_WORKSPACE;
   if (tc128_configure() != cudaSuccess) return QRB200_ERR_CUDA;
-  const cudaError_t e = launch_wide(H, (long long)n * n, H, Y, ws, batch, (int)n, 0, kOB, 0, (int)n,
+  const cudaError_t e = launch_wide(H, (long long)n * n, H, Tt, ws.Y, ws, batch, (int)n, 0, kOB, 0, (int)n,
                                     static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
 }

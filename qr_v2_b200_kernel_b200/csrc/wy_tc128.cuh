@@ -38,10 +38,11 @@ struct TbuildParams {
 };
 // T's strictly lower part is zero, so it holds the Gram blocks the recurrence reads instead:
 // G[i][j] (block(i) < block(j)) lives at T[j][i]; and each step's intermediate X sits in the
-// block column T[0:r, r:r+32] that the step then overwrites with its result. 66 KB: three CTAs
-// per SM.
+// block column T[0:r, r:r+32] that the step then overwrites with its result. Rows are 132 floats
+// apart so that four consecutive columns form one aligned float4; 66 KB: three CTAs per SM.
+constexpr int kTbLd = kOB + 4;
 struct TbuildShared {
-  float T[kOB][kOB + 1];
+  float T[kOB][kTbLd];
 };
 constexpr size_t kTbuildSmem = sizeof(TbuildShared);
 
@@ -81,55 +82,94 @@ __global__ void __launch_bounds__(256, 3) tbuild_kernel(TbuildParams P) {
   }
   cp_async_wait<0>();
   __syncthreads();
-  // Register-tiled block steps: thread (ti, tj) owns rows ti + 8 q (q < r/8... up to 12) of
-  // column tj of the new 32-column block, so every shared load feeds several independent
-  // FMA chains.
-  const int tj = tid & 31, ti = tid >> 5;  // 32 columns x 8 row phases
+  // Register-tiled block steps: thread (ti, tj) owns rows ti nq .. ti nq + nq - 1 (nq = r / 8:
+  // 4, 8 or 12 consecutive rows) of column tj of the new 32-column block. Its rows of a column
+  // of G or T are one or more float4 loads shared by the whole warp (same ti), so every shared
+  // load feeds four to twelve FMAs instead of one.
+  const int tj = tid & 31, ti = tid >> 5;  // 32 columns x 8 row groups
   for (int bb = 1; bb * 32 < ow; ++bb) {
     const int r = 32 * bb;  // rows of the new column block
     const int nq = r / 8;   // rows per thread: 4, 8 or 12
-    // X = G[0:r, r:r+32] T_bb     (T_bb upper triangular: c <= tj), into T[0:r, r:r+32]
+    const int i0 = ti * nq;
+    // X = G[0:r, r:r+32] T_bb into T[0:r, r:r+32]. T_bb is upper triangular with zeros stored
+    // below its diagonal, so the sum runs over all 32 rows of it (the extra terms are exact zeros).
     {
       float acc[12];
 #pragma unroll
       for (int q = 0; q < 12; ++q) acc[q] = 0.f;
-      for (int c = 0; c <= tj; ++c) {
+#pragma unroll 4
+      for (int c = 0; c < 32; ++c) {
         const float t = sh.T[r + c][r + tj];
+        const float* gc = &sh.T[r + c][i0];  // G[i0 + q][r + c], stored transposed
 #pragma unroll
-        for (int q = 0; q < 12; ++q)
-          if (q < nq) acc[q] = fmaf(sh.T[r + c][ti + 8 * q], t, acc[q]);  // G[ti + 8q][r + c]
+        for (int q4 = 0; q4 < 3; ++q4) {
+          if (4 * q4 < nq) {
+            const float4 g4 = *reinterpret_cast<const float4*>(gc + 4 * q4);
+            acc[4 * q4 + 0] = fmaf(g4.x, t, acc[4 * q4 + 0]);
+            acc[4 * q4 + 1] = fmaf(g4.y, t, acc[4 * q4 + 1]);
+            acc[4 * q4 + 2] = fmaf(g4.z, t, acc[4 * q4 + 2]);
+            acc[4 * q4 + 3] = fmaf(g4.w, t, acc[4 * q4 + 3]);
+          }
+        }
       }
+      // X goes to rows 0 .. r - 1, which this phase does not read.
 #pragma unroll
       for (int q = 0; q < 12; ++q)
-        if (q < nq) sh.T[ti + 8 * q][r + tj] = acc[q];
+        if (q < nq) sh.T[i0 + q][r + tj] = acc[q];
     }
     __syncthreads();
-    // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r, 0:r] upper triangular: c >= row)
+    // T[0:r, r:r+32] = -T[0:r, 0:r] X   (T[0:r, 0:r] upper triangular: c >= row; its storage
+    // below the diagonal holds Gram entries, masked here)
     {
       float acc[12];
 #pragma unroll
       for (int q = 0; q < 12; ++q) acc[q] = 0.f;
-      for (int c = ti; c < r; ++c) {
-        const float x = sh.T[c][r + tj];
+      // The first nq columns meet the thread's own rows (masked); beyond them every term counts.
+      for (int c = i0; c < i0 + nq; c += 4) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = sh.T[c + e][r + tj];
 #pragma unroll
         for (int q = 0; q < 12; ++q) {
-          const int i = ti + 8 * q;
-          if (q < nq && c >= i) acc[q] = fmaf(sh.T[i][c], x, acc[q]);
+          if (q < nq) {
+            const int i = i0 + q;
+            const float4 t4 = *reinterpret_cast<const float4*>(&sh.T[i][c]);
+            acc[q] = fmaf(c + 0 >= i ? t4.x : 0.f, x[0], acc[q]);
+            acc[q] = fmaf(c + 1 >= i ? t4.y : 0.f, x[1], acc[q]);
+            acc[q] = fmaf(c + 2 >= i ? t4.z : 0.f, x[2], acc[q]);
+            acc[q] = fmaf(c + 3 >= i ? t4.w : 0.f, x[3], acc[q]);
+          }
+        }
+      }
+      for (int c = i0 + nq; c < r; c += 4) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[e] = sh.T[c + e][r + tj];
+#pragma unroll
+        for (int q = 0; q < 12; ++q) {
+          if (q < nq) {
+            const float4 t4 = *reinterpret_cast<const float4*>(&sh.T[i0 + q][c]);
+            acc[q] = fmaf(t4.x, x[0], acc[q]);
+            acc[q] = fmaf(t4.y, x[1], acc[q]);
+            acc[q] = fmaf(t4.z, x[2], acc[q]);
+            acc[q] = fmaf(t4.w, x[3], acc[q]);
+          }
         }
       }
       __syncthreads();  // every thread is done reading X
 #pragma unroll
       for (int q = 0; q < 12; ++q)
-        if (q < nq) sh.T[ti + 8 * q][r + tj] = -acc[q];
+        if (q < nq) sh.T[i0 + q][r + tj] = -acc[q];
     }
     __syncthreads();
   }
   // Upper triangle of the first ow columns; the Gram storage below the diagonal and any block
   // column the recurrence did not reach are zero in T.
+  // Stored row by row (coalesced); the transposed form reads shared memory transposed instead.
   for (int e = tid; e < kOB * kOB; e += 256) {
-    const int i = e / kOB, j = e % kOB;
-    const float v = (i > j || j >= ow) ? 0.f : sh.T[i][j];
-    P.Tout[(long long)b * kOB * kOB + (P.transpose ? j * kOB + i : e)] = v;
+    const int oi = e / kOB, oj = e % kOB;
+    const int i = P.transpose ? oj : oi, j = P.transpose ? oi : oj;  // element T[i][j]
+    P.Tout[(long long)b * kOB * kOB + e] = (i > j || j >= ow) ? 0.f : sh.T[i][j];
   }
 }
 
@@ -139,7 +179,12 @@ __global__ void __launch_bounds__(256, 3) tbuild_kernel(TbuildParams P) {
 //   MODE_Y  : P = V T^T  -> Y rows   (A = V rows of H, unit lower; B rows = T rows)
 //   MODE_UPD: P = Y W    -> C -= P   (A = Y rows; B rows = trailing columns, sum of the
 //                                     row-split partials W^T[col][0:128])
-enum Gemm128Mode { MODE_Y = 0, MODE_UPD = 1 };
+// MODE_Y   : Y = V T^T (rows of V)                  -> Y
+// MODE_UPD : C -= Y W  (B = one or two W^T partials) -> C
+// MODE_WT  : W'^T = W^T T (rows = trailing columns; A = one or two W^T partials, B = T^T rows),
+//            so that W' = T^T V^T C                   -> the W'^T buffer (P.Y)
+// MODE_UPDV: C -= V W' (A = V rows of H, B = W'^T)    -> C
+enum Gemm128Mode { MODE_Y = 0, MODE_UPD = 1, MODE_WT = 2, MODE_UPDV = 3 };
 
 struct Gemm128Params {
   const float* H;         // matrices (V source for MODE_Y; C destination for MODE_UPD)

@@ -35,14 +35,19 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const int tid = threadIdx.x, warp = tid >> 5;
   const int bidx = blockIdx.z;
   const int n = P.n, k = P.k, w = P.w, m = n - k;
-  const int ncols = (MODE == MODE_Y) ? kOB : P.cend - k - w;
-  const int col0 = (MODE == MODE_UPD ? P.coff : 0) + blockIdx.x * 128, row0 = blockIdx.y * 128;
+  constexpr bool kStore = (MODE == MODE_Y || MODE == MODE_WT);  // P to a buffer, not C -= P
+  constexpr bool kUpd = !kStore;
+  constexpr bool kAV = (MODE == MODE_Y || MODE == MODE_UPDV);    // A = V rows of H
+  const int ncols = kStore ? kOB : P.cend - k - w;
+  const int mrows = (MODE == MODE_WT) ? P.cend - k - w : m;      // valid A rows
+  const int col0 = (kUpd ? P.coff : 0) + blockIdx.x * 128, row0 = (MODE == MODE_WT ? P.coff : 0) + blockIdx.y * 128;
   const int ldc = P.ldc > 0 ? P.ldc : n, ccol = P.ldc > 0 ? P.ccol : k + w;
   const long long hob = P.ldc > 0 ? P.hout_bstride : (long long)n * n;
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
-  const float* __restrict__ Bsrc = (MODE == MODE_Y) ? P.T + (long long)bidx * kOB * kOB
-                                                    : P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB;
+  const float* __restrict__ Bsrc = (MODE == MODE_Y || MODE == MODE_WT) ? P.T + (long long)bidx * kOB * kOB
+                                   : (MODE == MODE_UPDV ? Yb : P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB);
+  const float* __restrict__ Wsrc = P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB;  // MODE_WT's A
 
   if (tid == 0) {
 #pragma unroll
@@ -56,7 +61,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const uint32_t tmem = sh.tmem;
   constexpr uint32_t idesc = make_idesc_tf32(128, 128, false, false);
   bool ok = true;
-  if (MODE == MODE_UPD && row0 + tid < m) {
+  if (kUpd && row0 + tid < m) {
     // The epilogue's slice of C (this thread's row, 128 columns) starts moving HBM -> L2 now,
     // under the K loop, instead of after it.
     const float* crow = P.src + (long long)bidx * P.src_bstride + (long long)(k + row0 + tid) * ldc + ccol + col0;
@@ -85,9 +90,12 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
       const int c = kc * kGChunk + 4 * cq;
       const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
       const int r = row0 + rr;
-      const bool va = r < m && c < w;
-      const float* sa = (MODE == MODE_Y) ? Hb + (long long)(k + r) * n + k + c : Yb + (long long)r * kOB + c;
+      const bool va = r < mrows && c < w;
+      const float* sa = kAV ? Hb + (long long)(k + r) * n + k + c
+                            : (MODE == MODE_WT ? Wsrc : Yb) + (long long)r * kOB + c;
       cp_async16(st.a_hi + off, va ? sa : Hb, va);
+      if (MODE == MODE_WT && P.nsplit == 2)  // second row-split partial, parked in a_lo
+        cp_async16(st.a_lo + off, va ? Wsrc + (long long)P.ncmax * kOB + (long long)r * kOB + c : Hb, va);
       const int j = col0 + rr;
       const bool vb = j < ncols && c < w;
       cp_async16(st.b_hi + off, vb ? Bsrc + (long long)j * kOB + c : Bsrc, vb);
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
       int rr, cq;
       coord(it, rr, cq);
       const uint32_t off = tile_off(rr, 4 * cq, RS, CS) >> 2;
-      if (MODE == MODE_Y && row0 == 0) {
+      if (kAV && row0 == 0) {
         // V is unit lower trapezoidal: rows <= column hold R in H.
         const int r = rr, c = kc * kGChunk + 4 * cq;
         float4 x = *reinterpret_cast<const float4*>(st.a_hi + off);
@@ -133,7 +141,19 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
         if (c >= w) x = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(st.a_hi + off) = x;
       }
-      split_inplace(st.a_hi, st.a_lo, off);
+      if (MODE == MODE_WT && P.nsplit == 2) {  // W^T = partial 0 + partial 1, then split
+        const float4 x0 = *reinterpret_cast<const float4*>(st.a_hi + off);
+        const float4 x1 = *reinterpret_cast<const float4*>(st.a_lo + off);
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        x.x += x0.x; x.y += x0.y; x.z += x0.z; x.w += x0.w;
+        x.x += x1.x; x.y += x1.y; x.z += x1.z; x.w += x1.w;
+        float4 h, l;
+        split4(x, h, l);
+        *reinterpret_cast<float4*>(st.a_hi + off) = h;
+        *reinterpret_cast<float4*>(st.a_lo + off) = l;
+      } else {
+        split_inplace(st.a_hi, st.a_lo, off);
+      }
       if (MODE == MODE_UPD && P.nsplit == 2) {  // W = partial 0 + partial 1, then split
         const float4 x0 = *reinterpret_cast<const float4*>(st.b_hi + off);
         const float4 x1 = *reinterpret_cast<const float4*>(st.b_lo + off);
@@ -178,13 +198,13 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = row0 + 32 * warp + 4 * i + lr;
-      cv[i] = (MODE == MODE_UPD && r < m && c < ncols)
+      cv[i] = (kUpd && r < m && c < ncols)
                   ? *reinterpret_cast<const float4*>(Sb + (long long)(k + r) * ldc + ccol + c)
                   : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
   float4 cA[8], cB[8];
-  if (MODE == MODE_UPD) load_chunk(0, cA);
+  if (kUpd) load_chunk(0, cA);
   {
     const int last = NK - 1;
     ok = mbar_wait(&sh.mbar[last % kPipeSlots], (uint32_t)((last / kPipeSlots) & 1)) && ok;
@@ -201,14 +221,14 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
     __syncwarp();
     float4 (&cur)[8] = (q & 1) ? cB : cA;
     float4 (&nxt)[8] = (q & 1) ? cA : cB;
-    if (MODE == MODE_UPD && q + 1 < 4) load_chunk(q + 1, nxt);
+    if (kUpd && q + 1 < 4) load_chunk(q + 1, nxt);
     const int c = col0 + q * 32 + 4 * lq;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rl = 4 * i + lr, r = row0 + 32 * warp + rl;
       const float4 p = *reinterpret_cast<const float4*>(stg + rl * kPad + 4 * lq);
-      if (!ok || r >= m || c >= ncols) continue;
-      if (MODE == MODE_Y) {
+      if (!ok || r >= mrows || c >= ncols) continue;
+      if (kStore) {
         *reinterpret_cast<float4*>(P.Y + (long long)bidx * P.y_bstride + (long long)r * kOB + c) = p;
       } else {
         *reinterpret_cast<float4*>(Ho + (long long)(k + r) * ldc + ccol + c) =
