@@ -353,10 +353,25 @@ static cudaError_t launch_panel_for(const PanelParams& pp, int m, long long batc
     if (m <= 256) return launch_fw<8>(q, batch, s);
     return launch_fw<16>(q, batch, s);
   }
-  if (m <= 128) return launch_owner<4>(q, batch, s);
-  if (m <= 256) return launch_owner<8>(q, batch, s);
-  if (m <= 384) return launch_owner<12>(q, batch, s);
-  return launch_owner<16>(q, batch, s);
+  // Owner panels hold exactly ceil(m / 32) rows per lane: no padding rows to carry.
+  switch ((m + 31) / 32) {
+    case 1: return launch_owner<1>(q, batch, s);
+    case 2: return launch_owner<2>(q, batch, s);
+    case 3: return launch_owner<3>(q, batch, s);
+    case 4: return launch_owner<4>(q, batch, s);
+    case 5: return launch_owner<5>(q, batch, s);
+    case 6: return launch_owner<6>(q, batch, s);
+    case 7: return launch_owner<7>(q, batch, s);
+    case 8: return launch_owner<8>(q, batch, s);
+    case 9: return launch_owner<9>(q, batch, s);
+    case 10: return launch_owner<10>(q, batch, s);
+    case 11: return launch_owner<11>(q, batch, s);
+    case 12: return launch_owner<12>(q, batch, s);
+    case 13: return launch_owner<13>(q, batch, s);
+    case 14: return launch_owner<14>(q, batch, s);
+    case 15: return launch_owner<15>(q, batch, s);
+    default: return launch_owner<16>(q, batch, s);
+  }
 }
 
 // Kernel kind of the panel launch for a panel of m rows (cluster panels counted apart).
