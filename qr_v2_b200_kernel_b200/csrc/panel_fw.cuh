@@ -45,6 +45,7 @@ struct __align__(16) PanelFwShared {
   float Rb[8][4][32];   // rows 0..31 of every factored block as written to H (R entries above V)
   float G[32][33];      // Gram entries V_a^T V_b (a < b blocks); then the T recurrence's Y
   float T[32][33];
+  float tau[32];        // the factor warp's tau, written to global memory after its last block
   int vcount, bflag[2], gcount[8];
 };
 
@@ -256,7 +257,9 @@ __global__ void __launch_bounds__(32 * kPanelFwWarps) panel_fw_kernel(PanelParam
         fw_apply_rowmajor<R, RPL>(a, sh.Vr[(t - 1) & 1], &sh.Tb[t - 1][0][0]);  // V_{t-1}
       }
       float Tw[4][4];
-      fw_factor_block<4, RPL, true>(a, c0, jmax, Tw, taub);
+      // tau stays in shared memory: a global store here would hold up the fence of the
+      // block's publication below (a fence waits for the thread's global stores).
+      fw_factor_block<4, RPL, true>(a, c0, jmax, Tw, sh.tau);
       // V_t masked (rows >= 32 lie below every pivot of the panel), in both layouts.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -281,6 +284,8 @@ __global__ void __launch_bounds__(32 * kPanelFwWarps) panel_fw_kernel(PanelParam
           for (int c = 0; c < 4; ++c) sh.Tb[t][kk][c] = Tw[kk][c];
       fw_publish(&sh.vcount, t + 1);
     }
+    __syncwarp();  // lane 0 wrote tau
+    if (lane < jmax) taub[lane] = sh.tau[lane];
   } else if ((w & 3) != 0) {
     // ---------------- update warps ----------------
     // Warp u owns block t = u + 1: it applies V_0 .. V_{t-2} and hands the block over; then,
