@@ -209,12 +209,14 @@ _chunk_streams: dict[int, list] = {}
 
 def _host_chunks(batch: int, n: int) -> int:
     """Pieces a host-buffer call is cut into, by input size: one below 32 MB (the copies are
-    short), two below 192 MB, else four; at most one per matrix. Each piece runs on its own
-    stream with its own look-ahead streams, so the pieces' factorisations overlap one another
-    as well as the copies (measured on B200: C4 e2e 9.97 -> 8.27 ms with two pieces, C5 14.8 ->
-    13.3 ms, C3 11.0 -> 10.0 ms with four)."""
+    short), two below 192 MB, four below 512 MB, else eight; at most one per matrix. Each piece
+    runs on its own stream with its own look-ahead streams, so the pieces' factorisations
+    overlap one another as well as the copies, and the call ends one piece's factorisation and
+    copy-out after the last input byte arrives (measured on B200: C4 e2e 9.97 -> 8.27 ms with
+    two pieces, C5 14.8 -> 13.3 ms, C3 11.0 -> 10.0 ms with four, C2 17.8 -> 16.3 ms with eight;
+    more pieces than that lost: C3 10.0 ms with eight, C4 10.3 ms with four)."""
     nbytes = 4 * batch * n * n
-    k = 1 if nbytes < (32 << 20) else (2 if nbytes < (192 << 20) else 4)
+    k = 1 if nbytes < (32 << 20) else (2 if nbytes < (192 << 20) else (4 if nbytes < (512 << 20) else 8))
     return max(1, min(k, batch))
 
 
@@ -229,7 +231,7 @@ def _streams(device: torch.device, count: int) -> list:
 def custom_kernel_host(data: torch.Tensor, device=None, out=None, chunks: int | None = None):
     """Batched QR of a host-resident ``(batch, n, n)`` float32 tensor, results back on the host.
 
-    The batch is cut into up to four contiguous pieces, each on its own CUDA stream of
+    The batch is cut into up to eight contiguous pieces, each on its own CUDA stream of
     ``device`` (default: the current device): copy in, factor (:func:`custom_kernel`), copy out,
     so the copies of one piece overlap the factorisations of the others, and the pieces'
     factorisations overlap one another (use pinned host memory for that). Every matrix is factored exactly as :func:`custom_kernel` would factor it (a

@@ -108,7 +108,7 @@ def test_host_api_rejects_bad_inputs_on_cpu():
     # pieces by input size: one below 32 MB, two below 192 MB, else four; at most one per matrix
     assert _host_chunks(8, 128) == 1  # C1: 0.5 MB
     assert _host_chunks(8, 2048) == 2 and _host_chunks(2, 4096) == 2  # C4, C5: 134 MB
-    assert _host_chunks(64, 1024) == 4 and _host_chunks(640, 512) == 4  # C3, C2
+    assert _host_chunks(64, 1024) == 4 and _host_chunks(640, 512) == 8  # C3: 268 MB, C2: 671 MB
     assert _host_chunks(1, 4096) == 1  # never more pieces than matrices
 
 
