@@ -140,7 +140,7 @@ struct OwnerShared {
 
 template <int RPL, int CPW, bool HAS_T>
 __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const int w, const int jmax,
-                                                   OwnerShared<RPL, CPW>& sh, float* __restrict__ tau_out) {
+                                                   OwnerShared<RPL, CPW>& sh) {
   constexpr int NW = 32 / CPW;
   const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
   // Reflector j = NW oq + jg is owned by warp jg as its register column oq. The loop over oq is
@@ -172,10 +172,7 @@ __device__ __forceinline__ void factor_panel_owner(float (&a)[CPW][RPL], const i
           sh.v[ph][lr] = vi;
           a[oq][i] = (lr > j) ? vi : (lr == j ? rf.diag : a[oq][i]);
         }
-        if (lane == 0) {
-          sh.tau[j] = rf.tau;
-          tau_out[j] = rf.tau;
-        }
+        if (lane == 0) sh.tau[j] = rf.tau;  // to global memory after the loop
       }
       __syncthreads();
       const float tj = sh.tau[j];
@@ -247,7 +244,7 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 12 ? 3 : 
     for (int i = 0; i < RPL; ++i) a[q][i] = stage[c * (R + 1) + lane + 32 * i];
   }
   __syncthreads();
-  factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
+  factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh);
   __syncthreads();  // every warp is done reading the stage; sh.tiny is final
   if (sh.tiny) {
     // A squared norm fell below 2^-100, where the squares lose digits to the subnormal range
@@ -276,7 +273,7 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 12 ? 3 : 
 #pragma unroll
         for (int i = 0; i < RPL; ++i) a[q][i] = stage[(g + NW * q) * (R + 1) + lane + 32 * i] * scl;
       __syncthreads();
-      factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh, P.tau + (long long)bidx * n + k);
+      factor_panel_owner<RPL, CPW, HAS_T>(a, w, min(w, m), sh);
 #pragma unroll
       for (int q = 0; q < CPW; ++q)
 #pragma unroll
@@ -292,6 +289,7 @@ __global__ void __launch_bounds__(32 * (32 / CPW), (CPW >= 4 ? (RPL <= 12 ? 3 : 
     for (int i = 0; i < RPL; ++i) stage[c * (R + 1) + lane + 32 * i] = a[q][i];
   }
   __syncthreads();  // staged panel, Gram entries and tau are complete
+  if (g == 0 && lane < min(w, m)) P.tau[(long long)bidx * n + k + lane] = sh.tau[lane];
   if (HAS_T && g == 0) {
     // Warp 0 builds and stores T while the other warps write the panel.
     larft_inverse_warp(sh.T, sh.G, sh.tau, min(w, m));
