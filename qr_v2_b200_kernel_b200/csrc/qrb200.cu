@@ -11,6 +11,8 @@
 //                     panel's columns updated on a high-priority stream (U1), the rest (U2) on
 //                     a low-priority one beside the next panel;
 //   rows not 16-byte aligned (n % 4 != 0 or an unaligned input): single-level, one stream.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -31,6 +33,7 @@
 #include "wy_u1.cuh"
 #include "wy_tc128.cuh"
 #include "wy_tc128p.cuh"
+#include "wy_tc128t.cuh"
 #include "apply_q.cuh"
 
 namespace qrb200 {
@@ -444,6 +447,7 @@ static cudaError_t tc128_configure() {
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_WT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPDV, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(tc_upd_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tma_upd_smem())) != cudaSuccess) return e;
   done.mark(dev);
   return cudaSuccess;
 }
@@ -649,6 +653,36 @@ static cudaError_t lookahead_streams(LaSlot& slot, LookaheadStreams** out) {
   return cudaSuccess;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map over a batch of row-major float matrices (cols x rows x batch; row and matrix strides
+// in bytes, multiples of 16), box 4 columns x 128 rows: what tc_upd_tma_kernel loads per piece.
+// Rows and columns past the extents read as zero.
+static bool encode_rows_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint64_t batch,
+                            uint64_t row_bytes, uint64_t mat_bytes) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {cols, rows, batch};
+  const cuuint64_t strides[2] = {row_bytes, mat_bytes};
+  const cuuint32_t box[3] = {4, 128, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 128-wide update of trailing columns [coff, cend - k0 - ow) (relative to k0 + ow) by the
 // outer block at k0, whose T factor is given transposed (Tt, batch x 128 x 128):
 //   W^T = C^T V per row split (tc_vtc128), W'^T = W^T T, i.e. W' = T^T V^T C (tc_tw128, into Wt,
@@ -708,7 +742,11 @@ static cudaError_t launch_wide(const float* src, long long sbs, float* H, const 
   {
     LaunchScope ls(K_UPD128, 2.0 * bm * ow * nc, 8.0 * bm * nc + 4.0 * bm * ow + 4.0 * batch * ow * (double)nc);
     const dim3 grid(cdiv(nc, 128), cdiv(m, 128), (unsigned)batch);
-    tc_gemm128_pipe_kernel<MODE_UPDV, 3><<<grid, 128, pipe128_smem<3>(), s>>>(gp);
+    CUtensorMap tmV, tmW;
+    if (!encode_rows_map(&tmV, H, n, n, batch, 4ull * n, 4ull * n * n) ||
+        !encode_rows_map(&tmW, Wt, kOB, n, batch, 4ull * kOB, 4ull * n * kOB))
+      return cudaErrorInvalidValue;
+    tc_upd_tma_kernel<<<grid, 128, tma_upd_smem(), s>>>(gp, tmV, tmW);
   }
   return cudaGetLastError();
 }
