@@ -446,7 +446,6 @@ static cudaError_t tc128_configure() {
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPD, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_Y, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_WT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(tc_gemm128_pipe_kernel<MODE_UPDV, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pipe128_smem<3>())) != cudaSuccess) return e;
   if ((e = cudaFuncSetAttribute(tc_upd_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tma_upd_smem())) != cudaSuccess) return e;
   done.mark(dev);
   return cudaSuccess;

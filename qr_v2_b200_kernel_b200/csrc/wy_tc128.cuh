@@ -183,8 +183,8 @@ __global__ void __launch_bounds__(256, 3) tbuild_kernel(TbuildParams P) {
 // MODE_UPD : C -= Y W  (B = one or two W^T partials) -> C
 // MODE_WT  : W'^T = W^T T (rows = trailing columns; A = one or two W^T partials, B = T^T rows),
 //            so that W' = T^T V^T C                   -> the W'^T buffer (P.Y)
-// MODE_UPDV: C -= V W' (A = V rows of H, B = W'^T)    -> C
-enum Gemm128Mode { MODE_Y = 0, MODE_UPD = 1, MODE_WT = 2, MODE_UPDV = 3 };
+// (C -= V W', A = V rows of H and B = W'^T, is tc_upd_tma_kernel in wy_tc128t.cuh.)
+enum Gemm128Mode { MODE_Y = 0, MODE_UPD = 1, MODE_WT = 2 };
 
 struct Gemm128Params {
   const float* H;         // matrices (V source for MODE_Y; C destination for MODE_UPD)

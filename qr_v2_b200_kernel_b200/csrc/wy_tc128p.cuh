@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const int n = P.n, k = P.k, w = P.w, m = n - k;
   constexpr bool kStore = (MODE == MODE_Y || MODE == MODE_WT);  // P to a buffer, not C -= P
   constexpr bool kUpd = !kStore;
-  constexpr bool kAV = (MODE == MODE_Y || MODE == MODE_UPDV);    // A = V rows of H
+  constexpr bool kAV = (MODE == MODE_Y);                         // A = V rows of H
   const int ncols = kStore ? kOB : P.cend - k - w;
   const int mrows = (MODE == MODE_WT) ? P.cend - k - w : m;      // valid A rows
   const int col0 = (kUpd ? P.coff : 0) + blockIdx.x * 128, row0 = (MODE == MODE_WT ? P.coff : 0) + blockIdx.y * 128;
@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(128) tc_gemm128_pipe_kernel(Gemm128Params P) {
   const float* __restrict__ Hb = P.H + (long long)bidx * n * n;
   const float* __restrict__ Yb = P.Y + (long long)bidx * P.y_bstride;
   const float* __restrict__ Bsrc = (MODE == MODE_Y || MODE == MODE_WT) ? P.T + (long long)bidx * kOB * kOB
-                                   : (MODE == MODE_UPDV ? Yb : P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB);
+                                                                       : P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB;
   const float* __restrict__ Wsrc = P.Wp + (long long)bidx * P.nsplit * P.ncmax * kOB;  // MODE_WT's A
 
   if (tid == 0) {

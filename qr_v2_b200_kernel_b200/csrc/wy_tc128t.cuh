@@ -8,8 +8,9 @@
 // into the K-major core-matrix layout the MMA reads (masking V to its unit lower trapezoid in the
 // block's first 128 rows). Row-major boxes of natural strides keep the tensor maps plain; the
 // quad-major landing makes both the converter's reads and its writes conflict-free.
-// Three slots, loads one stage ahead, two CTAs per SM, the MMAs, arithmetic and epilogue of
-// tc_gemm128_pipe_kernel<MODE_UPDV>, so the two agree bit for bit.
+// Three slots, loads one stage ahead, two CTAs per SM. The tiles, MMAs, 3xTF32 arithmetic and
+// the staged epilogue are those of tc_gemm128_pipe_kernel<MODE_UPD> (wy_tc128p.cuh) with V in
+// place of Y.
 #pragma once
 
 #include <cuda.h>
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(128) tc_upd_tma_kernel(Gemm128Params P, const 
       mma_commit(&sh.mbar[kc % S]);
     }
   }
-  // Epilogue as tc_gemm128_pipe_kernel's: each 32-column chunk of the product goes through a
+  // Epilogue as tc_gemm128_pipe_kernel<MODE_UPD>'s: each 32-column chunk of the product goes through a
   // padded shared tile so that global traffic runs along rows; the next chunk's C is in flight
   // while the current one is processed.
   const int lane = tid & 31, lr = lane >> 3, lq = lane & 7;
