@@ -27,14 +27,21 @@ namespace qrb200 {
 
 constexpr int kU1Rows = 256, kU1Ld = 36, kU1Threads = 512;
 
+// The row-eighth partials are dead once they are summed into W, which happens before the first
+// cluster barrier; the buffers written after it share their space, so that two CTAs fit on an
+// SM (112 KB each).
 struct __align__(16) U1Shared {
   float V[kU1Rows][kU1Ld];
   float C[kU1Rows][kU1Ld];
-  float Wq[8][32][32];  // row-eighth partials
-  float W[32][32];      // this CTA's partial V^T C, read by the peers
-  float Wh[32][32];     // sum of the upper half of the peers' partials
-  float Wt[32][33];     // the cluster total
-  float W2[32][32];     // T^T W
+  union {
+    float Wq[8][32][32];  // row-eighth partials
+    struct {
+      float Wh[32][32];   // sum of the upper half of the peers' partials
+      float Wt[32][33];   // the cluster total
+      float W2[32][32];   // T^T W
+    } s;
+  } u;
+  float W[32][32];        // this CTA's partial V^T C, read by the peers
   float T[32][33];
 };
 constexpr size_t kU1Smem = sizeof(U1Shared);
@@ -119,15 +126,15 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
     }
 #pragma unroll
     for (int a = 0; a < 4; ++a)
-      *reinterpret_cast<float4*>(&sh.Wq[rq][4 * ig + a][4 * cg]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(&sh.u.Wq[rq][4 * ig + a][4 * cg]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
   }
   __syncthreads();
   const int i = (tid >> 3) & 31, cq = tid & 7, half = tid >> 8;
   if (half == 0) {
-    float4 s = *reinterpret_cast<const float4*>(&sh.Wq[0][i][4 * cq]);
+    float4 s = *reinterpret_cast<const float4*>(&sh.u.Wq[0][i][4 * cq]);
 #pragma unroll
     for (int q = 1; q < 8; ++q) {
-      const float4 t = *reinterpret_cast<const float4*>(&sh.Wq[q][i][4 * cq]);
+      const float4 t = *reinterpret_cast<const float4*>(&sh.u.Wq[q][i][4 * cq]);
       s.x += t.x;
       s.y += t.y;
       s.z += t.z;
@@ -154,14 +161,14 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
       tot.z += part[q].z;
       tot.w += part[q].w;
     }
-    if (half == 1) *reinterpret_cast<float4*>(&sh.Wh[i][4 * cq]) = tot;
+    if (half == 1) *reinterpret_cast<float4*>(&sh.u.s.Wh[i][4 * cq]) = tot;
     __syncthreads();
     if (half == 0) {
-      const float4 hi = *reinterpret_cast<const float4*>(&sh.Wh[i][4 * cq]);
-      sh.Wt[i][4 * cq] = tot.x + hi.x;
-      sh.Wt[i][4 * cq + 1] = tot.y + hi.y;
-      sh.Wt[i][4 * cq + 2] = tot.z + hi.z;
-      sh.Wt[i][4 * cq + 3] = tot.w + hi.w;
+      const float4 hi = *reinterpret_cast<const float4*>(&sh.u.s.Wh[i][4 * cq]);
+      sh.u.s.Wt[i][4 * cq] = tot.x + hi.x;
+      sh.u.s.Wt[i][4 * cq + 1] = tot.y + hi.y;
+      sh.u.s.Wt[i][4 * cq + 2] = tot.z + hi.z;
+      sh.u.s.Wt[i][4 * cq + 3] = tot.w + hi.w;
     }
   }
   __syncthreads();
@@ -170,9 +177,9 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
     for (int c = 0; c <= i; ++c) {
       const float t = sh.T[c][i];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) y[e] = fmaf(t, sh.Wt[c][4 * cq + e], y[e]);
+      for (int e = 0; e < 4; ++e) y[e] = fmaf(t, sh.u.s.Wt[c][4 * cq + e], y[e]);
     }
-    *reinterpret_cast<float4*>(&sh.W2[i][4 * cq]) = make_float4(y[0], y[1], y[2], y[3]);
+    *reinterpret_cast<float4*>(&sh.u.s.W2[i][4 * cq]) = make_float4(y[0], y[1], y[2], y[3]);
   }
   __syncthreads();
   // (4) C_p - V_p W2: row tid % 256, columns 16 (tid / 256) .. + 15, back through shared memory.
@@ -195,7 +202,7 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
       for (int a = 0; a < 4; ++a) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float4 y = *reinterpret_cast<const float4*>(&sh.W2[c4 + a][cb + 4 * q]);
+          const float4 y = *reinterpret_cast<const float4*>(&sh.u.s.W2[c4 + a][cb + 4 * q]);
           out[4 * q] = fmaf(-vv[a], y.x, out[4 * q]);
           out[4 * q + 1] = fmaf(-vv[a], y.y, out[4 * q + 1]);
           out[4 * q + 2] = fmaf(-vv[a], y.z, out[4 * q + 2]);
