@@ -571,7 +571,7 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     if (vec && ncl > kU3Cols) {
       const int tc = cdiv(ncl, kU4Cols), tr = cdiv(m, kU4Rows);
       const long long nt = (long long)tc * tr * batch;
-      note(launch_k(wy_upd4_kernel, dim3((unsigned)nt), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr, (int)nt));
+      note(launch_k(wy_upd4_kernel, dim3((unsigned)nt), dim3(256), kUpd4Smem, s, 0, true, wp, tc, tr));
     } else if (vec && ncl <= 32) {
       const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
       const long long nt = (long long)tc * tr * batch;

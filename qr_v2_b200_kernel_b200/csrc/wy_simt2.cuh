@@ -7,7 +7,7 @@
 //                    outputs per thread;
 //   wy_vtcn_kernel : the same for updates of 32 or 64 columns;
 //   wy_tw2_kernel  : W2 = T^T sum_s Wp[s];
-//   wy_upd3_kernel / wy_upd4_kernel : C <- C - V W2 over persistent tiles, cp.async rings.
+//   wy_upd3_kernel : C <- C - V W2 over persistent tiles, cp.async ring; wy_upd4_kernel: one tile per CTA.
 // Same arithmetic per output as wy_simt.cuh except for the summation order inside each
 // partial product.
 #pragma once
@@ -398,25 +398,21 @@ struct Upd4Stage {
   float V[kU4Rows][32];
   float W[32][kU4Cols];
 };
-constexpr size_t kUpd4Smem = sizeof(Upd4Stage) * 2;
+// One 64 x 128 tile per CTA (57 KB: several CTAs per SM, so one CTA's loads overlap another's
+// arithmetic; a persistent grid that filled every SM held the next high-priority panel back).
+constexpr size_t kUpd4Smem = sizeof(Upd4Stage);
 
-__global__ void __launch_bounds__(256) wy_upd4_kernel(WyParams P, int tiles_c, int tiles_r, int ntiles) {
+// C -= V W2 for tile blockIdx.x (matrix-major, then row tiles, then column tiles).
+__global__ void __launch_bounds__(256) wy_upd4_kernel(WyParams P, int tiles_c, int tiles_r) {
   griddep_launch_wait();
   extern __shared__ __align__(16) unsigned char u4_smem_raw[];
-  Upd4Stage* st = reinterpret_cast<Upd4Stage*>(u4_smem_raw);
+  Upd4Stage& s = *reinterpret_cast<Upd4Stage*>(u4_smem_raw);
   const int n = P.n, k = P.k, w = P.w, m = n - k, nc = P.cend - k - w;
   const int tid = threadIdx.x, cg = tid & 15, rg = tid >> 4;
-  auto tile_of = [&](int t, int& b, int& row0, int& col0) {
-    const int per_b = tiles_c * tiles_r;
-    b = t / per_b;
-    const int rem = t - b * per_b;
-    row0 = (rem / tiles_c) * kU4Rows;
-    col0 = P.coff + (rem % tiles_c) * kU4Cols;
-  };
-  auto issue = [&](int t, int slot) {
-    int b, row0, col0;
-    tile_of(t, b, row0, col0);
-    Upd4Stage& s = st[slot];
+  const int t = blockIdx.x, per_b = tiles_c * tiles_r;
+  const int b = t / per_b, rem = t - b * per_b;
+  const int row0 = (rem / tiles_c) * kU4Rows, col0 = P.coff + (rem % tiles_c) * kU4Cols;
+  {
     const float* __restrict__ Sb = P.src + (long long)b * P.src_bstride;
     const float* __restrict__ Hb = P.H + (long long)b * n * n;
     const float* __restrict__ W2b = P.W2 + (long long)b * 32 * P.ncmax;
@@ -438,77 +434,64 @@ __global__ void __launch_bounds__(256) wy_upd4_kernel(WyParams P, int tiles_c, i
       const bool ok = col < nc;
       cp_async16(&s.W[c][4 * q], ok ? W2b + (long long)c * P.ncmax + col : W2b, ok);
     }
-  };
-  int t = blockIdx.x;
-  if (t < ntiles) issue(t, 0);
-  cp_async_commit();
-  for (int it = 0; t < ntiles; t += gridDim.x, ++it) {
-    const int slot = it & 1;
-    const int tn = t + gridDim.x;
-    if (tn < ntiles) issue(tn, slot ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    int b, row0, col0;
-    tile_of(t, b, row0, col0);
-    Upd4Stage& s = st[slot];
-    if (row0 == 0) {
-      // Panel rows 0..31: V is unit lower triangular there.
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int e = q * 256 + tid, rr = e >> 5, c = e & 31;
-        const float v = s.V[rr][c];
-        s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
-      }
-      __syncthreads();
-    }
-    // acc[i][h]: row 4 rg + i, column pair h of this thread's eight (h < 2: 4 cg + 2 h ..;
-    // h >= 2: 64 + 4 cg + 2 (h - 2) ..).
-    float2 acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int h = 0; h < 4; ++h) acc[i][h] = make_float2(0.f, 0.f);
-#pragma unroll 2
-    for (int c4 = 0; c4 < 32; c4 += 4) {
-      float4 vr[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) vr[i] = *reinterpret_cast<const float4*>(&s.V[4 * rg + i][c4]);
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const float4 xa = *reinterpret_cast<const float4*>(&s.W[c4 + cc][4 * cg]);
-        const float4 xb = *reinterpret_cast<const float4*>(&s.W[c4 + cc][64 + 4 * cg]);
-        const float2 xp[4] = {make_float2(xa.x, xa.y), make_float2(xa.z, xa.w), make_float2(xb.x, xb.y),
-                              make_float2(xb.z, xb.w)};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float v = cc == 0 ? vr[i].x : (cc == 1 ? vr[i].y : (cc == 2 ? vr[i].z : vr[i].w));
-          const float2 vv = make_float2(v, v);
-#pragma unroll
-          for (int h = 0; h < 4; ++h) acc[i][h] = __ffma2_rn(vv, xp[h], acc[i][h]);
-        }
-      }
-    }
-    float* __restrict__ Ho = P.H + (long long)b * n * n;
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int cl = 64 * hh + 4 * cg, col = col0 + cl;
-      if (col < nc) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = row0 + 4 * rg + i;
-          if (r < m) {
-            const float4 c = *reinterpret_cast<const float4*>(&s.C[4 * rg + i][cl]);
-            *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
-                make_float4(c.x - acc[i][2 * hh].x, c.y - acc[i][2 * hh].y, c.z - acc[i][2 * hh + 1].x,
-                            c.w - acc[i][2 * hh + 1].y);
-          }
-        }
-      }
-    }
-    __syncthreads();  // the slot is refilled by the next iteration's issue
   }
+  cp_async_commit();
   cp_async_wait<0>();
+  __syncthreads();
+  if (row0 == 0) {
+    // Panel rows 0..31: V is unit lower triangular there.
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = q * 256 + tid, rr = e >> 5, c = e & 31;
+      const float v = s.V[rr][c];
+      s.V[rr][c] = (c >= w) ? 0.f : (rr > c ? v : (rr == c ? 1.f : 0.f));
+    }
+    __syncthreads();
+  }
+  // acc[i][h]: row 4 rg + i, column pair h of this thread's eight (h < 2: 4 cg + 2 h ..;
+  // h >= 2: 64 + 4 cg + 2 (h - 2) ..).
+  float2 acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int h = 0; h < 4; ++h) acc[i][h] = make_float2(0.f, 0.f);
+#pragma unroll 2
+  for (int c4 = 0; c4 < 32; c4 += 4) {
+    float4 vr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) vr[i] = *reinterpret_cast<const float4*>(&s.V[4 * rg + i][c4]);
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const float4 xa = *reinterpret_cast<const float4*>(&s.W[c4 + cc][4 * cg]);
+      const float4 xb = *reinterpret_cast<const float4*>(&s.W[c4 + cc][64 + 4 * cg]);
+      const float2 xp[4] = {make_float2(xa.x, xa.y), make_float2(xa.z, xa.w), make_float2(xb.x, xb.y),
+                            make_float2(xb.z, xb.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float v = cc == 0 ? vr[i].x : (cc == 1 ? vr[i].y : (cc == 2 ? vr[i].z : vr[i].w));
+        const float2 vv = make_float2(v, v);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) acc[i][h] = __ffma2_rn(vv, xp[h], acc[i][h]);
+      }
+    }
+  }
+  float* __restrict__ Ho = P.H + (long long)b * n * n;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const int cl = 64 * hh + 4 * cg, col = col0 + cl;
+    if (col < nc) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = row0 + 4 * rg + i;
+        if (r < m) {
+          const float4 c = *reinterpret_cast<const float4*>(&s.C[4 * rg + i][cl]);
+          *reinterpret_cast<float4*>(Ho + (long long)(k + r) * n + k + w + col) =
+              make_float4(c.x - acc[i][2 * hh].x, c.y - acc[i][2 * hh].y, c.z - acc[i][2 * hh + 1].x,
+                          c.w - acc[i][2 * hh + 1].y);
+        }
+      }
+    }
+  }
 }
 
 }  // namespace qrb200
