@@ -468,6 +468,11 @@ static int num_sms() {
   return v;
 }
 
+// CTAs of the persistent update kernels (wy_upd3 64 x 64, 128 x 32) resident per SM, from the
+// occupancy query when the kernels are configured on a device: their grids are that many CTAs per
+// SM, so that no CTA of a persistent grid waits for another to finish its whole share of tiles.
+static int g_upd3_resident[kMaxDevicesSm][2];
+
 // Compact-WY update of columns [k + w + coff, cend) by the 32-column panel at k (the narrow
 // update inside an outer block, or either half of a single-level look-ahead update). T factors
 // sit t_bstride elements apart. Aligned rows: a short update (<= 128 columns, allow_u1) is one
@@ -522,7 +527,17 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tc_vtcw_pipe_kernel<32, false, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)vtcw_pipe_smem<32, false, 3>());
+      int r64 = 0, r128 = 0;
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r64, wy_upd3_kernel<kU3Rows, kU3Cols>, 256,
+                                                          upd3_smem<kU3Rows, kU3Cols>());
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r128, wy_upd3_kernel<128, 32>, 256, upd3_smem<128, 32>());
       if (e != cudaSuccess) return e;
+      if (dev < kMaxDevicesSm) {
+        g_upd3_resident[dev][0] = std::max(1, r64);
+        g_upd3_resident[dev][1] = std::max(1, r128);
+      }
       configured.mark(dev);
     }
   }
@@ -575,12 +590,16 @@ static cudaError_t launch_wy(const float* src, long long sbs, float* H, const fl
     } else if (vec && ncl <= 32) {
       const int tc = cdiv(ncl, 32), tr = cdiv(m, 128);
       const long long nt = (long long)tc * tr * batch;
-      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+      const int dev = current_device();
+      const long long res = dev < kMaxDevicesSm && g_upd3_resident[dev][1] > 0 ? g_upd3_resident[dev][1] : 2;
+      const int grid = (int)std::min<long long>(nt, res * num_sms());
       note(launch_k(wy_upd3_kernel<128, 32>, dim3(grid), dim3(256), upd3_smem<128, 32>(), s, 0, true, wp, tc, tr, (int)nt));
     } else if (vec) {
       const int tc = cdiv(ncl, kU3Cols), tr = cdiv(m, kU3Rows);
       const long long nt = (long long)tc * tr * batch;
-      const int grid = (int)std::min<long long>(nt, 3LL * num_sms());
+      const int dev = current_device();
+      const long long res = dev < kMaxDevicesSm && g_upd3_resident[dev][0] > 0 ? g_upd3_resident[dev][0] : 3;
+      const int grid = (int)std::min<long long>(nt, res * num_sms());
       note(launch_k(wy_upd3_kernel<kU3Rows, kU3Cols>, dim3(grid), dim3(256), upd3_smem<kU3Rows, kU3Cols>(), s, 0, true, wp, tc, tr, (int)nt));
     } else {
       wy_upd_kernel<kNB><<<dim3(cdiv(ncl, 64), cdiv(m, 64), (unsigned)batch), 256, 0, s>>>(wp);
