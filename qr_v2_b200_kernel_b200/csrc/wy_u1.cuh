@@ -14,7 +14,7 @@
 //   (3) after one cluster barrier adds the CP partials from the peers' shared memory in rank
 //       order (two halves of the peers read by two thread halves, then added: every CTA gets
 //       bitwise the same W) and forms W2 = T^T W,
-//   (4) writes C_p - V_p W2 back (two threads per row, 16 columns each, through shared memory).
+//   (4) writes C_p - V_p W2 back (4 x 4 blocks per thread in shared memory, then coalesced).
 // A second cluster barrier keeps every CTA's partial readable until all peers are done.
 #pragma once
 
@@ -108,25 +108,28 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
   __syncthreads();
   // (2) partial W over the slab: thread (rq, ig, cg) sums rows rq, rq + 8, ... for a 4 x 4 block.
   {
+    // Paired FMAs (two independent, individually rounded fmaf per instruction).
     const int cg = tid & 7, ig = (tid >> 3) & 7, rq = tid >> 6;
-    float acc[4][4];
+    float2 acc[4][2];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int a = 0; a < 4; ++a) acc[a][0] = acc[a][1] = make_float2(0.f, 0.f);
 #pragma unroll 4
     for (int r = rq; r < kU1Rows; r += 8) {
       const float4 v = *reinterpret_cast<const float4*>(&sh.V[r][4 * ig]);
       const float4 x = *reinterpret_cast<const float4*>(&sh.C[r][4 * cg]);
-      const float vv[4] = {v.x, v.y, v.z, v.w}, xx[4] = {x.x, x.y, x.z, x.w};
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      const float2 x01 = make_float2(x.x, x.y), x23 = make_float2(x.z, x.w);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(vv[a], xx[b], acc[a][b]);
+      for (int a = 0; a < 4; ++a) {
+        const float2 va = make_float2(vv[a], vv[a]);
+        acc[a][0] = __ffma2_rn(va, x01, acc[a][0]);
+        acc[a][1] = __ffma2_rn(va, x23, acc[a][1]);
+      }
     }
 #pragma unroll
     for (int a = 0; a < 4; ++a)
-      *reinterpret_cast<float4*>(&sh.u.Wq[rq][4 * ig + a][4 * cg]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(&sh.u.Wq[rq][4 * ig + a][4 * cg]) =
+          make_float4(acc[a][0].x, acc[a][0].y, acc[a][1].x, acc[a][1].y);
   }
   __syncthreads();
   const int i = (tid >> 3) & 31, cq = tid & 7, half = tid >> 8;
@@ -182,37 +185,40 @@ __global__ void __launch_bounds__(kU1Threads) wy_u1_kernel(WyParams P) {
     *reinterpret_cast<float4*>(&sh.u.s.W2[i][4 * cq]) = make_float4(y[0], y[1], y[2], y[3]);
   }
   __syncthreads();
-  // (4) C_p - V_p W2: row tid % 256, columns 16 (tid / 256) .. + 15, back through shared memory.
+  // (4) C_p - V_p W2: thread (row group rg = tid / 8, column quad cg = tid % 8) updates rows
+  // rg + 64 i (i < 4) of its four columns in place in the staged C (a 4 x 4 register block,
+  // paired FMAs, columns of V in order), then the slab goes back through shared memory.
   {
-    const int row = tid & (kU1Rows - 1), cb = 16 * half;
-    float out[16];
+    const int rg = tid >> 3, cg = tid & 7;
+    float2 acc[4][2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 x = *reinterpret_cast<const float4*>(&sh.C[row][cb + 4 * q]);
-      out[4 * q] = x.x;
-      out[4 * q + 1] = x.y;
-      out[4 * q + 2] = x.z;
-      out[4 * q + 3] = x.w;
+    for (int r = 0; r < 4; ++r) {
+      const float4 x = *reinterpret_cast<const float4*>(&sh.C[rg + 64 * r][4 * cg]);
+      acc[r][0] = make_float2(x.x, x.y);
+      acc[r][1] = make_float2(x.z, x.w);
     }
 #pragma unroll 2
     for (int c4 = 0; c4 < 32; c4 += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(&sh.V[row][c4]);
-      const float vv[4] = {v.x, v.y, v.z, v.w};
+      float4 vr[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) vr[r] = *reinterpret_cast<const float4*>(&sh.V[rg + 64 * r][c4]);
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
+        const float4 y = *reinterpret_cast<const float4*>(&sh.u.s.W2[c4 + a][4 * cg]);
+        const float2 y01 = make_float2(y.x, y.y), y23 = make_float2(y.z, y.w);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 y = *reinterpret_cast<const float4*>(&sh.u.s.W2[c4 + a][cb + 4 * q]);
-          out[4 * q] = fmaf(-vv[a], y.x, out[4 * q]);
-          out[4 * q + 1] = fmaf(-vv[a], y.y, out[4 * q + 1]);
-          out[4 * q + 2] = fmaf(-vv[a], y.z, out[4 * q + 2]);
-          out[4 * q + 3] = fmaf(-vv[a], y.w, out[4 * q + 3]);
+        for (int r = 0; r < 4; ++r) {
+          const float v = -(a == 0 ? vr[r].x : (a == 1 ? vr[r].y : (a == 2 ? vr[r].z : vr[r].w)));
+          const float2 vv = make_float2(v, v);
+          acc[r][0] = __ffma2_rn(vv, y01, acc[r][0]);
+          acc[r][1] = __ffma2_rn(vv, y23, acc[r][1]);
         }
       }
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      *reinterpret_cast<float4*>(&sh.C[row][cb + 4 * q]) = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    for (int r = 0; r < 4; ++r)
+      *reinterpret_cast<float4*>(&sh.C[rg + 64 * r][4 * cg]) =
+          make_float4(acc[r][0].x, acc[r][0].y, acc[r][1].x, acc[r][1].y);
   }
   __syncthreads();
 #pragma unroll
