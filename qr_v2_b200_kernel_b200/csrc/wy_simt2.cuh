@@ -55,11 +55,11 @@ __global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
     }
   };
 
-  float acc[4][4];
+  // acc[i][h]: output row 4 ty + i, columns 4 tx + 2 h and the next (paired FMAs: two
+  // independent, individually rounded fmaf per instruction).
+  float2 acc[4][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int s = 0; s < kV2Stages - 1; ++s) {
     if (s < nchunks) issue(s);
@@ -85,11 +85,14 @@ __global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
     for (int rr = 0; rr < kV2Rows; ++rr) {
       const float4 v = *reinterpret_cast<const float4*>(&s.V[rr][4 * ty]);
       const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * tx]);
-      const float vv[4] = {v.x, v.y, v.z, v.w}, cc[4] = {c.x, c.y, c.z, c.w};
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      const float2 c01 = make_float2(c.x, c.y), c23 = make_float2(c.z, c.w);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], cc[e], acc[i][e]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 vi = make_float2(vv[i], vv[i]);
+        acc[i][0] = __ffma2_rn(vi, c01, acc[i][0]);
+        acc[i][1] = __ffma2_rn(vi, c23, acc[i][1]);
+      }
     }
   }
   cp_async_wait<0>();
@@ -99,7 +102,7 @@ __global__ void __launch_bounds__(256) wy_vtc2_kernel(WyParams P) {
 #pragma unroll
     for (int i = 0; i < 4; ++i)
       *reinterpret_cast<float4*>(out + (long long)(4 * ty + i) * P.ncmax + col) =
-          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+          make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
   }
 }
 
@@ -269,11 +272,11 @@ __global__ void __launch_bounds__(256) wy_vtcn_kernel(WyParams P) {
     }
   };
 
-  float acc[4][4];
+  // acc[i][h]: output row 4 ty + i, columns 4 tx + 2 h and the next (paired FMAs: two
+  // independent, individually rounded fmaf per instruction).
+  float2 acc[4][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int s = 0; s < kV2Stages - 1; ++s) {
     if (s < nchunks) issue(s);
@@ -298,18 +301,21 @@ __global__ void __launch_bounds__(256) wy_vtcn_kernel(WyParams P) {
     for (int rr = ph; rr < kV2Rows; rr += NPH) {
       const float4 v = *reinterpret_cast<const float4*>(&s.V[rr][4 * ty]);
       const float4 c = *reinterpret_cast<const float4*>(&s.C[rr][4 * tx]);
-      const float vv[4] = {v.x, v.y, v.z, v.w}, cc[4] = {c.x, c.y, c.z, c.w};
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+      const float2 c01 = make_float2(c.x, c.y), c23 = make_float2(c.z, c.w);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[i][e] = fmaf(vv[i], cc[e], acc[i][e]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 vi = make_float2(vv[i], vv[i]);
+        acc[i][0] = __ffma2_rn(vi, c01, acc[i][0]);
+        acc[i][1] = __ffma2_rn(vi, c23, acc[i][1]);
+      }
     }
   }
   cp_async_wait<0>();
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     *reinterpret_cast<float4*>(&red[(ph * 32 + 4 * ty + i) * COLS + 4 * tx]) =
-        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
   __syncthreads();
   // Threads of phase 0 add the phases in order and store.
   if (ph == 0) {
