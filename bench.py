@@ -150,17 +150,38 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.skip = 0
+
+    def _rows(self) -> list:
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        return rows
 
     def start(self):
+        """Start sampling every 25 ms and return once the first sample is written (at most 5 s),
+        so that the sampler is running when the timed region begins; samples taken before that
+        are left out of the summary (a multi-GPU timed region can be shorter than 0.1 s)."""
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu), "-lms", "200"],
+                 "-i", str(self.gpu), "-lms", "25"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            n = len(self._rows())
+            if n > 0:
+                self.skip = n
+                break
+            time.sleep(0.01)
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -170,12 +191,11 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        rows = self._rows()
         os.unlink(self.path)
+        # Samples taken inside the timed region; if it ended before the next sample, the one
+        # written just before it began.
+        rows = rows[self.skip:] or rows[-1:]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
 
